@@ -1,0 +1,163 @@
+"""Generate the golden fixtures by running the REFERENCE itself (its PyTorch op bodies and its PyTorch beam
+bookkeeping, on CPU) on the seeded cases of ``cases.py``.
+
+Run where the reference source tree is importable (it does not travel to the GPU box; the fixtures do):
+
+    python tests/golden/make_golden.py [--reference-src <path to the reference's src/ directory>]
+
+Writes ``attn_golden.npz`` (attention outputs + input digests) and ``slots_golden.npz`` (per-step search states
+before/after the reference's bookkeeping) next to this script.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+import zlib
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import cases  # noqa: E402
+
+STATE_FIELDS = ("t", "pos", "sot_pos", "no_speech", "done", "hist", "cum", "src", "tokens", "forced", "h_count",
+                "h_score", "h_len", "h_tokens", "last_t")
+
+
+SPLIT_STORED = ("split_s5_f32", "config1_f32")
+
+
+def attn_golden(ap) -> dict:
+    out = {}
+    for name, (kind, kw) in cases.ATTN_CASES.items():
+        inp = cases.make_attn_inputs(kind, kw)
+        out[f"{name}/digest"] = np.array(cases.inputs_digest(inp))
+        if "qkv" in inp:
+            f = {k: inp[k].float() for k in ("qkv", "kc", "vc")}
+            y = ap.self_attn(f["qkv"], f["kc"], f["vc"], inp["offset"], inp["src"])
+            out[f"{name}/self"] = y.numpy()
+            if kind == "plugin_step":  # the write variant's offsets (test_attn_plugin.py:60)
+                off40 = torch.full_like(inp["offset"], 40)
+                out[f"{name}/self_off40"] = ap.self_attn(f["qkv"], f["kc"], f["vc"], off40, inp["src"]).numpy()
+        if "q" in inp:
+            q, k, v = inp["q"].float(), inp["xk"].float(), inp["xv"].float()
+            out[f"{name}/cross"] = ap.cross_attn(q, k, v).numpy()
+            if name in SPLIT_STORED:  # (the partials are large: stored for the small-head cases only)
+                part = ap.cross_attn_split(q, k, v)
+                out[f"{name}/part"] = part.numpy()
+                out[f"{name}/combined"] = ap.cross_attn_combine(part, q).numpy()
+    return out
+
+
+# --- the beam bookkeeping: the reference Search (PyTorch bookkeeping, CPU) with a fake decoder ----------------
+V, EOT, SOT, NOSPEECH = 40, 1, 2, 3
+
+
+def _scores_of(history, seed):
+    g = torch.Generator().manual_seed(zlib.crc32(repr((seed, history)).encode()))
+    x = torch.randn(V, generator=g, dtype=torch.float64) * 2.5
+    x[EOT] += 0.15 * len(history)
+    return x
+
+
+def _fake_step(seed):
+    """test_search.py:34-48's fake decoder: cache values are token ids, read back through ``src``."""
+
+    def step_fn(tokens, offset, cache, logits, new_kv, src):
+        def run():
+            for n in range(tokens.shape[0]):
+                off = int(offset[n])
+                hist = [int(round(float(cache[0, 0, int(src[n, j]), 0, j, 0]))) for j in range(off)]
+                for s in range(tokens.shape[1]):
+                    tok = int(tokens[n, s])
+                    logits[n, s] = _scores_of(hist + [tok], seed).float()
+                    new_kv[0, :, n, 0, s, :] = float(tok)
+                    hist.append(tok)
+
+        return run
+
+    return step_fn
+
+
+def slots_golden(ref_src: str) -> dict:
+    from whisper_trt.config import WhisperConfig
+    from whisper_trt.search import Search
+
+    cfg = WhisperConfig(n_mels=4, d_model=4, enc_layers=1, enc_heads=1, enc_ffn=4, dec_layers=1, dec_heads=1,
+                        dec_ffn=4, vocab_size=V, eot=EOT, sot=SOT, no_speech=NOSPEECH)
+    out = {}
+    step_no = 0
+    for run, (K, seed, prefilled) in enumerate([(3, 0, False), (5, 1, False), (3, 2, True)]):
+        W, M = 3, 7
+        suppress, begin = [5, 6, 7], [8, EOT]
+        if prefilled:
+            prompts = [[4 + (w * 7 + j) % 30 for j in range(3 * w)] + [SOT, 10 + w, 20, 30] for w in range(M)]
+            search = Search(cfg, _fake_step(seed), W, K, None, "beam", dtype=torch.float32, device="cpu",
+                            max_length=40, graphs=False, fused=False)
+        else:
+            prompts = [[SOT, 10 + w, 20 + w % 3, 30] for w in range(M)]
+            search = Search(cfg, _fake_step(seed), W, K, 4, "beam", dtype=torch.float32, device="cpu",
+                            max_length=40, graphs=False, fused=False)
+        rec = {}
+        orig_beam, orig_body = search._beam, search._body
+
+        def beam(logp, prompt, s=search, orig=orig_beam, rec=rec):
+            scores = (logp + s.cum[:, None]).view(s.B, s.K * s.cfg.vocab_size)
+            top_s, top_i = scores.topk(2 * s.K, dim=1)
+            rec["top_s"], rec["top_i"] = top_s.clone(), top_i.clone()
+            orig(logp, prompt)
+
+        def body(s=search, orig=orig_body, rec=rec):
+            nonlocal step_no
+            before = {f: getattr(s, f).clone() for f in STATE_FIELDS}
+            orig()
+            after = {f: getattr(s, f).clone() for f in STATE_FIELDS}
+            lg = s.logits[:: s.K, 0]
+            ns = (lg[:, s.cfg.no_speech] - lg.logsumexp(-1)).exp()
+            key = f"step{step_no:04d}"
+            for f in STATE_FIELDS:
+                out[f"{key}/before/{f}"] = before[f].numpy()
+                out[f"{key}/after/{f}"] = after[f].numpy()
+            out[f"{key}/top_s"] = rec["top_s"].numpy()
+            out[f"{key}/top_i"] = rec["top_i"].numpy()
+            out[f"{key}/ns"] = ns.numpy()
+            out[f"{key}/meta"] = np.array([K, search.P, V, EOT, run], dtype=np.int64)
+            step_no += 1
+
+        search._beam = beam
+        search._body = body
+        if prefilled:
+            def prefill(slots, ps, s=search):
+                for sl, p in zip(slots, ps):
+                    row = sl * s.K
+                    for j, tok in enumerate(p[:-1]):
+                        s.cache[0, :, row, 0, j, :] = float(tok)
+
+            search.stream(prompts, lambda slots, windows: None, suppress, begin, check_every=1, ahead=1,
+                          prefill=prefill)
+        else:
+            search.stream(prompts, lambda slots, windows: None, suppress, begin, check_every=1, ahead=1)
+    return out
+
+
+def main() -> None:
+    ap_ = argparse.ArgumentParser()
+    ap_.add_argument("--reference-src", default="/root/reference/src")
+    args = ap_.parse_args()
+    sys.path.insert(0, args.reference_src)
+    from whisper_trt import attn_plugin
+
+    attn_plugin.RUNTIME_TRITON = False
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    a = attn_golden(attn_plugin)
+    np.savez_compressed(HERE / "attn_golden.npz", **a)
+    s = slots_golden(args.reference_src)
+    np.savez_compressed(HERE / "slots_golden.npz", **s)
+    print(f"attn cases: {len(cases.ATTN_CASES)}; bookkeeping steps: {sum(k.endswith('/meta') for k in s)}")
+
+
+if __name__ == "__main__":
+    main()
