@@ -1,0 +1,145 @@
+/*
+ * whisper_attn_b200 -- the Whisper decoder's per-step attention for B200 (sm_100a), as a C ABI.
+ *
+ * One shared library (libwhisper_attn_b200.so) with plain pointers and sizes: no torch types. Every entry point
+ * launches asynchronously on the given CUDA stream (a cudaStream_t passed as void*; NULL = the legacy default
+ * stream), never synchronises, never allocates, and is safe to record into a CUDA graph. Each returns a status
+ * (WT_OK = 0); on failure wt_last_error() gives the calling thread's message. Device code never traps: offsets
+ * are clamped to [0, C] and slot-table entries to [0, N-1], as the reference's kernels do.
+ *
+ * Element types: WT_F16 or WT_BF16 for every activation / cache tensor of a call. Every pointer must be 16-byte
+ * aligned (checked). Layouts are the reference plugin's (contiguous, row-major):
+ *   qkv      [N, 3*H*D]      queries, keys, values of the new token, heads in order
+ *   k/v cache [N, H, C, D]   one layer's self-attention cache (capacity C)
+ *   offset   [N]  int64      cached positions of each row (the new token's slot)
+ *   src      [N, C] int32    for each cache slot of a row, the row whose cache holds it
+ *   cross q  [W, S, H*D]     a window's S queries (its K beams x tokens), windows in order
+ *   cross k/v [W, H, T, D]   one layer's cross-attention keys/values (T encoder frames), once per window
+ *   part     [W, H, P, S, D+2] float32  split partials: unnormalised output, running max (log2 units), sum
+ *
+ * Reference interface each entry point replaces: Wataru-Nakata/whisper-trt, src/whisper_trt/attn_plugin.py and
+ * search.py / beam_kernels.py (file:line given per function).
+ */
+#ifndef WHISPER_ATTN_B200_H
+#define WHISPER_ATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WT_ABI_VERSION 1
+
+/* element types */
+#define WT_F16 0
+#define WT_BF16 1
+
+/* status codes */
+#define WT_OK 0
+#define WT_ERR_ARG 1         /* a size or pointer is invalid (null, negative, inconsistent) */
+#define WT_ERR_ALIGN 2       /* a pointer is not 16-byte aligned */
+#define WT_ERR_DTYPE 3       /* unknown element type */
+#define WT_ERR_UNSUPPORTED 4 /* a valid shape this build has no kernel for (e.g. head_dim not 64) */
+#define WT_ERR_WORKSPACE 5   /* workspace missing or smaller than the matching *_workspace() size */
+#define WT_ERR_CUDA 6        /* the CUDA launch failed */
+
+/* launch flags (wt_set_launch_flags) */
+#define WT_LAUNCH_PDL 1 /* programmatic dependent launch: a kernel may start while its predecessor drains */
+
+int wt_abi_version(void);
+const char *wt_status_string(int status);
+/* The message of the calling thread's last failing call ("" if none). */
+const char *wt_last_error(void);
+/* Process-wide launch flags (WT_LAUNCH_*); returns the previous value. Default: 0. */
+int wt_set_launch_flags(int flags);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Self-attention of one new token per row over the row's cache slots < offset[r], each read from the row
+ * src[r, j] names, plus the new token itself.
+ * Replaces attn_plugin.py:488-501 self_attn_step_triton (kernel :309-350, config :482-485).
+ *   y [N, 1, H*D] (element type of qkv) = softmax(q k^T / sqrt(D)) v over [gathered cache | new token].
+ *   write_cache != 0: the new key/value are also written into the row's own slot offset[r] (if < C) of
+ *   k_cache / v_cache (rows only read slots below their offset, so the result does not change).
+ *   kv_splits: 0 = choose from the shape; 1 = one CTA per (row, head); >1 = split every row's cache range over
+ *   that many CTAs combined in-kernel, which needs `workspace` of wt_self_attn_step_workspace() bytes.
+ *   A workspace is laid out by the call's shape (rows, heads, head_dim, kv_splits): zero it before its first use
+ *   with a shape; each call leaves its counters zeroed for the next call of the SAME shape (its partials stay as
+ *   written, so another shape needs another -- or a re-zeroed -- workspace). Calls that may overlap on the GPU
+ *   must not share a workspace.
+ * ------------------------------------------------------------------------------------------------------- */
+size_t wt_self_attn_step_workspace(int rows, int heads, int head_dim, int kv_splits);
+int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim);
+int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, const int64_t *offset,
+                      const int32_t *src, void *y, int rows, int heads, int capacity, int head_dim,
+                      int write_cache, int kv_splits, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Cross-attention, split over the T keys ("flash-decoding").
+ * wt_cross_attn_split replaces attn_plugin.py:521-534 cross_attn_split_triton (kernel :378-409): slice i of
+ *   chunk = ceil(T / splits) keys -> part[w, h, i, s, :] = (sum_j p_j v_j, m, sum_j p_j) with m the slice's
+ *   maximum score in log2 units and p_j = exp2(score_j - m); a slice without keys gets m = -inf, 0, 0.
+ * wt_cross_attn_combine replaces attn_plugin.py:537-546 cross_attn_combine_triton (kernel :411-435):
+ *   y [W, S, H*D] = sum_i w_i acc_i / sum_i w_i l_i with w_i = exp2(m_i - max m).
+ * wt_cross_attn replaces attn_plugin.py:504-518 cross_attn_triton (kernel :352-376): the same attention in one
+ *   launch (split + combine, the last CTA of each (window, head) combines); needs `workspace` of
+ *   wt_cross_attn_workspace() bytes, with the same per-shape rule as wt_self_attn_step's: zeroed before its
+ *   first use with a shape, valid for further calls of that shape only, not shared by calls that may overlap.
+ * ------------------------------------------------------------------------------------------------------- */
+int wt_cross_attn_split(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
+                        int queries, int heads, int frames, int head_dim, int splits, void *stream);
+int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, int queries, int heads,
+                          int head_dim, int splits, void *stream);
+size_t wt_cross_attn_workspace(int windows, int queries, int heads, int frames, int head_dim);
+int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *y, int windows, int queries,
+                  int heads, int frames, int head_dim, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * KV-cache append and gather (bit-exact copies).
+ * wt_cache_append: row r's new key/value (qkv[r, H*D:2*H*D], qkv[r, 2*H*D:]) into its own cache slot offset[r]
+ *   when 0 <= offset[r] < C. The append of attn_plugin.py:327-330 (WRITE) alone, i.e. the cache scatter of
+ *   search.py:249-250 for one layer and one token.
+ * wt_gather_cache: out[r, h, j, :] = cache[src[r, j], h, j, :] for every slot j < C (src clamped to [0, N-1]).
+ *   Replaces attn_plugin.py:92-99 gather_cache (the reference's materialised view of the slot table).
+ * ------------------------------------------------------------------------------------------------------- */
+int wt_cache_append(int dtype, const void *qkv, void *k_cache, void *v_cache, const int64_t *offset, int rows,
+                    int heads, int capacity, int head_dim, void *stream);
+int wt_gather_cache(int dtype, const void *cache, const int32_t *src, void *out, int rows, int heads,
+                    int capacity, int head_dim, void *stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Slot-table bookkeeping (integers, bit-exact). N = windows * beams rows; row r belongs to window r / beams.
+ * wt_beam_reorder: the new beams take their parents' slot tables, each marking the slot its parent wrote this
+ *   step: for each window b with live[b] != 0 (live may be NULL = all) and beam k with parent p = parent[b, k]
+ *   (0 <= p < beams): src[b*K+k] = src_old[b*K+p] and src[b*K+k, pos[b]] = b*K+p; with hist (may be NULL)
+ *   hist[b*K+k] = hist_old[b*K+p] and, when token and t are given, hist[b*K+k, t[b]] = token[b*K+k];
+ *   pos[b] += 1 when advance != 0; when offset (may be NULL) is given, offset[r] = pos[r / K] afterwards.
+ *   search.py:258 + :401-409 + :263-264 (beam_kernels.py:241-248, :260-264).
+ * wt_beam_update: beam_kernels.py:169-269 _update_kernel in beam mode (no sampled slots): from each window's
+ *   best 2K candidates (top_s, top_i = beam*V + token, best first) CTranslate2's rules -- finished hypotheses
+ *   registered, ended candidates replaced by the next non-ending secondary ones -- then the new beams' parents'
+ *   histories and slot tables, scores, tokens; prompt windows (t < 0) get their next prompt token and mark their
+ *   slot; windows not ending advance. State arrays as in the reference's Search (search.py:184-223).
+ * wt_slot_reset: search.py:440-446 (_start): for each of n_slots slots s (0 <= s < windows; others ignored),
+ *   rows s*K..s*K+K-1 read their own rows (src[r, :] = r) or, prefilled != 0, the slot's first row
+ *   (src[r, :] = s*K).
+ * Out-of-range parent / candidate indices are clamped to the window's beams, hypothesis slots beyond hyp_slots
+ * are not written: a bad index never touches another window or memory outside the arrays.
+ * ------------------------------------------------------------------------------------------------------- */
+int wt_beam_reorder(int32_t *src, int64_t *hist, const int64_t *token, const int64_t *t, const int64_t *parent,
+                    int64_t *pos, const uint8_t *live, int64_t *offset, int windows, int beams, int capacity,
+                    int hist_len, int advance, void *stream);
+int wt_beam_update(const float *top_s, const int64_t *top_i, int64_t *t, int64_t *pos, const int64_t *sot_pos,
+                   const float *ns, float *no_speech, uint8_t *done, int64_t *hist, float *cum, int32_t *src,
+                   int64_t *tokens, const int64_t *forced, int64_t *h_count, float *h_score, int64_t *h_len,
+                   int64_t *h_tokens, const int64_t *last_t, int windows, int beams, int capacity, int hist_len,
+                   int hyp_slots, int prompt_len, int vocab, int eot, void *stream);
+int wt_slot_reset(int32_t *src, const int64_t *slots, int n_slots, int windows, int beams, int capacity,
+                  int prefilled, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WHISPER_ATTN_B200_H */

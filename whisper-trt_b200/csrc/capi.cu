@@ -1,0 +1,51 @@
+// Status reporting and process-wide settings of the C ABI.
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace wt {
+
+namespace {
+thread_local char g_last_error[512] = "";
+std::atomic<int> g_launch_flags{0};
+}  // namespace
+
+int fail(int status, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int launch_flags() { return g_launch_flags.load(std::memory_order_relaxed); }
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace wt
+
+extern "C" {
+
+int wt_abi_version(void) { return WT_ABI_VERSION; }
+
+const char *wt_status_string(int status) {
+  switch (status) {
+    case WT_OK: return "ok";
+    case WT_ERR_ARG: return "invalid argument";
+    case WT_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case WT_ERR_DTYPE: return "unknown element type";
+    case WT_ERR_UNSUPPORTED: return "unsupported shape";
+    case WT_ERR_WORKSPACE: return "workspace missing or too small";
+    case WT_ERR_CUDA: return "CUDA launch failed";
+    default: return "unknown status";
+  }
+}
+
+const char *wt_last_error(void) { return wt::g_last_error; }
+
+int wt_set_launch_flags(int flags) { return wt::g_launch_flags.exchange(flags); }
+
+}  // extern "C"

@@ -1,0 +1,475 @@
+// Cross-attention of a window's queries (its beams / samples) over the window's encoder keys/values, split over
+// the keys ("flash-decoding"), with the split partials combined by a second kernel or inside the same launch.
+//
+// Semantics: the reference's _cross_split_kernel / _cross_combine_kernel / _cross_attn_kernel
+// (attn_plugin.py:352-435; reference bodies :129-194): scores in log2 units (scale d^-1/2 * log2 e), per key slice
+// i of chunk = ceil(T / splits): m = max, p = exp2(s - m), acc = sum p v, l = sum p; combined with weights
+// exp2(m_i - max m). fp16/bf16 inputs, fp32 accumulation.
+//
+// B200 design. HBM-bound (5 beams x 4 FLOP per key/value element pair: ~5 FLOP per byte). The one dense
+// contraction of the path, so it runs on the tensor cores with warp-level mma.sync.m16n8k16 (f32 accumulate):
+//   * S^T = K Q^T with the KEYS as the M dimension (16 per tile) and the window's queries as N (8 per tile, so 5
+//     beams waste 3/8 instead of 11/16 with queries as M), D = 64 as the reduction (4 k-steps);
+//   * O^T = V^T P^T with D as M (4 tiles) and the keys as the reduction;
+//   * no shared-memory staging and no ldmatrix: the operand fragments are loaded straight from HBM with coalesced
+//     16-byte loads. The key fragment uses a permutation of the head dimension (the same for the query
+//     fragment, so Q.K is unchanged) that gives every lane two 16-byte pieces of its key rows; the value
+//     fragment permutes D in the output (undone at the store) and pairs values of two keys with byte permutes;
+//   * P goes from the S^T accumulator layout to the P^T operand layout with one movmatrix.trans per 8x8 block;
+//     for bf16 inputs P is split into hi + lo bf16 parts (two mma) to keep ~16 bits of it.
+// One CTA of 4 warps per (window, head, key slice, query group); each warp streams 16-key blocks of the slice
+// with the next block's loads in flight while the current one is computed.
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace wt {
+namespace {
+
+constexpr int kCrossWarps = 4;
+constexpr int kCrossThreads = kCrossWarps * 32;
+constexpr int kD = 64;
+
+template <typename T> struct Mma;
+template <> struct Mma<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+};
+template <> struct Mma<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+};
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// The operands of one 16-key block for one lane (g = lane / 4, c = lane % 4):
+//   ka/kb: key rows g and g+8, head-dim pieces [8c, 8c+8) and [32+8c, 32+8c+8)
+//   v0..v3: value rows 2c, 2c+1, 2c+8, 2c+9, head-dim piece [8g, 8g+8)
+struct Block {
+  uint4 ka0, kb0, ka1, kb1, v0, v1, v2, v3;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_block(Block &b, const T *kb, const T *vb, int k0, int hi, int g, int c) {
+  const int last = hi - 1;
+  const int r0 = min(k0 + g, last), r8 = min(k0 + g + 8, last);
+  b.ka0 = ldg_stream(kb + static_cast<size_t>(r0) * kD + 8 * c);
+  b.kb0 = ldg_stream(kb + static_cast<size_t>(r0) * kD + 32 + 8 * c);
+  b.ka1 = ldg_stream(kb + static_cast<size_t>(r8) * kD + 8 * c);
+  b.kb1 = ldg_stream(kb + static_cast<size_t>(r8) * kD + 32 + 8 * c);
+  b.v0 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c, last)) * kD + 8 * g);
+  b.v1 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c + 1, last)) * kD + 8 * g);
+  b.v2 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c + 8, last)) * kD + 8 * g);
+  b.v3 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c + 9, last)) * kD + 8 * g);
+}
+
+template <int NT>
+struct State {
+  float m[NT][2], l[NT][2], o[NT][4][4];
+};
+
+template <typename T, int NT>
+__device__ __forceinline__ void compute_block(State<NT> &st, const Block &b, const uint32_t (&qf)[NT][8], int k0,
+                                              int hi, int g, float scale) {
+  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+  const bool ok0 = (k0 + g) < hi, ok8 = (k0 + g + 8) < hi;
+  // V^T operand fragments for the 4 head-dim tiles (shared by all query tiles)
+  uint32_t va[4][4];
+  const uint32_t w0[4] = {b.v0.x, b.v0.y, b.v0.z, b.v0.w}, w1[4] = {b.v1.x, b.v1.y, b.v1.z, b.v1.w};
+  const uint32_t w2[4] = {b.v2.x, b.v2.y, b.v2.z, b.v2.w}, w3[4] = {b.v3.x, b.v3.y, b.v3.z, b.v3.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    va[i][0] = __byte_perm(w0[i], w1[i], 0x5410);
+    va[i][1] = __byte_perm(w0[i], w1[i], 0x7632);
+    va[i][2] = __byte_perm(w2[i], w3[i], 0x5410);
+    va[i][3] = __byte_perm(w2[i], w3[i], 0x7632);
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    Mma<T>::run(sc, b.ka0.x, b.ka1.x, b.ka0.y, b.ka1.y, qf[nt][0], qf[nt][1]);
+    Mma<T>::run(sc, b.ka0.z, b.ka1.z, b.ka0.w, b.ka1.w, qf[nt][2], qf[nt][3]);
+    Mma<T>::run(sc, b.kb0.x, b.kb1.x, b.kb0.y, b.kb1.y, qf[nt][4], qf[nt][5]);
+    Mma<T>::run(sc, b.kb0.z, b.kb1.z, b.kb0.w, b.kb1.w, qf[nt][6], qf[nt][7]);
+    // sc: (key g, query 2c), (key g, query 2c+1), (key g+8, query 2c), (key g+8, query 2c+1)
+    const float s0 = ok0 ? sc[0] * scale : kNegInf, s1 = ok0 ? sc[1] * scale : kNegInf;
+    const float s2 = ok8 ? sc[2] * scale : kNegInf, s3 = ok8 ? sc[3] * scale : kNegInf;
+    float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(st.m[nt][0], mx0), mn1 = fmaxf(st.m[nt][1], mx1);  // finite: k0 < hi
+    const float a0 = exp2f(st.m[nt][0] - mn0), a1 = exp2f(st.m[nt][1] - mn1);
+    st.m[nt][0] = mn0;
+    st.m[nt][1] = mn1;
+    const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1), p2 = exp2f(s2 - mn0), p3 = exp2f(s3 - mn1);
+    const uint32_t h01 = Elem<T>::from_float2(p0, p1), h23 = Elem<T>::from_float2(p2, p3);
+    const float2 r01 = Elem<T>::to_float2(h01), r23 = Elem<T>::to_float2(h23);
+    float l0 = r01.x + r23.x, l1 = r01.y + r23.y;
+    uint32_t lo01 = 0, lo23 = 0;
+    if (kSplitP) {
+      lo01 = Elem<T>::from_float2(p0 - r01.x, p1 - r01.y);
+      lo23 = Elem<T>::from_float2(p2 - r23.x, p3 - r23.y);
+      const float2 q01 = Elem<T>::to_float2(lo01), q23 = Elem<T>::to_float2(lo23);
+      l0 += q01.x + q23.x;
+      l1 += q01.y + q23.y;
+    }
+    st.l[nt][0] = st.l[nt][0] * a0 + l0;
+    st.l[nt][1] = st.l[nt][1] * a1 + l1;
+    const uint32_t pb0 = movmatrix_trans(h01), pb1 = movmatrix_trans(h23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      st.o[nt][i][0] *= a0;
+      st.o[nt][i][1] *= a1;
+      st.o[nt][i][2] *= a0;
+      st.o[nt][i][3] *= a1;
+      Mma<T>::run(st.o[nt][i], va[i][0], va[i][1], va[i][2], va[i][3], pb0, pb1);
+    }
+    if (kSplitP) {
+      const uint32_t qb0 = movmatrix_trans(lo01), qb1 = movmatrix_trans(lo23);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Mma<T>::run(st.o[nt][i], va[i][0], va[i][1], va[i][2], va[i][3], qb0, qb1);
+    }
+  }
+}
+
+// Shared-memory layout of the CTA reduction: per warp, NT*8 queries x (64 outputs, m, l).
+template <int NT>
+constexpr int red_floats() {
+  return kCrossWarps * NT * 8 * (kD + 2);
+}
+
+// One CTA: (window, head) = blockIdx.x, key slice = blockIdx.y, query group = blockIdx.z.
+// FUSED = false: writes the reference's part[W, H, P, S, D+2] (slice partials).
+// FUSED = true: writes its partial to the workspace; the last CTA of the (window, head, query group) combines all
+// slices into y[W, S, H*D].
+template <typename T, int NT, bool FUSED>
+__global__ void __launch_bounds__(kCrossThreads)
+    cross_kernel(const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
+                 float *__restrict__ part, int *__restrict__ counters, T *__restrict__ y, int S, int H, int Tn,
+                 int P, float scale) {
+  __shared__ __align__(16) float red[red_floats<NT>()];
+  __shared__ int is_last;
+  const int wh = blockIdx.x, sp = blockIdx.y, qg = blockIdx.z, QG = gridDim.z;
+  const int w = wh / H, h = wh - w * H;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int chunk = (Tn + P - 1) / P;
+  const int lo = min(Tn, sp * chunk), hi = min(Tn, lo + chunk);
+  const size_t HD = static_cast<size_t>(H) * kD;
+  const T *kb = k + (static_cast<size_t>(w) * H + h) * Tn * kD;
+  const T *vb = v + (static_cast<size_t>(w) * H + h) * Tn * kD;
+  const int q0 = qg * NT * 8;
+
+  pdl_wait();
+
+  uint32_t qf[NT][8];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int qi = q0 + nt * 8 + g;
+    if (qi < S) {
+      const T *qp = q + (static_cast<size_t>(w) * S + qi) * HD + static_cast<size_t>(h) * kD;
+      const uint4 a = ldg16(qp + 8 * c), b = ldg16(qp + 32 + 8 * c);
+      qf[nt][0] = a.x; qf[nt][1] = a.y; qf[nt][2] = a.z; qf[nt][3] = a.w;
+      qf[nt][4] = b.x; qf[nt][5] = b.y; qf[nt][6] = b.z; qf[nt][7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qf[nt][i] = 0u;
+    }
+  }
+  State<NT> st;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    st.m[nt][0] = st.m[nt][1] = kNegInf;
+    st.l[nt][0] = st.l[nt][1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.o[nt][i][j] = 0.f;
+  }
+
+  // 16-key blocks of the slice, round-robin over the warps, two blocks in flight per warp
+  constexpr int kStride = kCrossWarps * 16;
+  int k0 = lo + warp * 16;
+  Block cur, nxt;
+  if (k0 < hi) load_block(cur, kb, vb, k0, hi, g, c);
+  while (k0 < hi) {
+    const int k1 = k0 + kStride;
+    if (k1 < hi) load_block(nxt, kb, vb, k1, hi, g, c);
+    compute_block<T, NT>(st, cur, qf, k0, hi, g, scale);
+    k0 = k1;
+    if (k0 >= hi) break;
+    const int k2 = k0 + kStride;
+    if (k2 < hi) load_block(cur, kb, vb, k2, hi, g, c);
+    compute_block<T, NT>(st, nxt, qf, k0, hi, g, scale);
+    k0 = k2;
+  }
+  pdl_launch_dependents();
+
+  // per-warp sums over the 8 lanes of each query column, then the CTA reduction in shared memory
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) st.l[nt][j] += __shfl_xor_sync(0xffffffffu, st.l[nt][j], o);
+  float *rw = red + warp * NT * 8 * (kD + 2);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float *rq = rw + (nt * 8 + 2 * c + j) * (kD + 2);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        rq[8 * g + 2 * i] = st.o[nt][i][j];      // head dim 8g+2i   (accumulator row g of tile i)
+        rq[8 * g + 2 * i + 1] = st.o[nt][i][j + 2];  // head dim 8g+2i+1 (row g+8)
+      }
+      if (g == 0) {
+        rq[kD] = st.m[nt][j];
+        rq[kD + 1] = st.l[nt][j];
+      }
+    }
+  }
+  __syncthreads();
+
+  const int nq = min(NT * 8, S - q0);  // queries of this CTA
+  // combine the warps: thread -> (query, head-dim pair)
+  float *outp = nullptr;
+  if (FUSED) {
+    outp = part + ((static_cast<size_t>(wh) * QG + qg) * P + sp) * (NT * 8) * (kD + 2);
+  }
+  for (int idx = tid; idx < nq * (kD / 2 + 1); idx += kCrossThreads) {
+    const int qq = idx / (kD / 2 + 1), dp = idx - qq * (kD / 2 + 1);
+    float top = kNegInf;
+#pragma unroll
+    for (int w2 = 0; w2 < kCrossWarps; ++w2) top = fmaxf(top, red[(w2 * NT * 8 + qq) * (kD + 2) + kD]);
+    float n0 = 0.f, n1 = 0.f, den = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < kCrossWarps; ++w2) {
+      const float *rq = red + (w2 * NT * 8 + qq) * (kD + 2);
+      const float mw = rq[kD];
+      const float wgt = (mw == kNegInf) ? 0.f : exp2f(mw - top);
+      if (dp < kD / 2) {
+        n0 = fmaf(wgt, rq[2 * dp], n0);
+        n1 = fmaf(wgt, rq[2 * dp + 1], n1);
+      } else {
+        den = fmaf(wgt, rq[kD + 1], den);
+      }
+    }
+    float *dst = FUSED ? outp + qq * (kD + 2)
+                       : part + (((static_cast<size_t>(wh) * P + sp) * S) + q0 + qq) * (kD + 2);
+    if (dp < kD / 2) {
+      dst[2 * dp] = n0;
+      dst[2 * dp + 1] = n1;
+    } else {
+      dst[kD] = top;
+      dst[kD + 1] = den;
+    }
+  }
+  if (!FUSED) return;
+
+  __threadfence();
+  __syncthreads();
+  const int unit = wh * QG + qg;
+  if (tid == 0) is_last = (atomicAdd(counters + unit, 1) == P - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const float *base = part + static_cast<size_t>(unit) * P * (NT * 8) * (kD + 2);
+  for (int idx = tid; idx < nq * (kD / 8); idx += kCrossThreads) {
+    const int qq = idx / (kD / 8), d8 = idx - qq * (kD / 8);
+    float top = kNegInf;
+    for (int s2 = 0; s2 < P; ++s2) top = fmaxf(top, __ldcg(base + (s2 * NT * 8 + qq) * (kD + 2) + kD));
+    float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
+    for (int s2 = 0; s2 < P; ++s2) {
+      const float *ps = base + (s2 * NT * 8 + qq) * (kD + 2);
+      const float ms = __ldcg(ps + kD);
+      const float wgt = (ms == kNegInf) ? 0.f : exp2f(ms - top);
+      den = fmaf(wgt, __ldcg(ps + kD + 1), den);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(ps + 8 * d8 + i), num[i]);
+    }
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) num[i] *= inv;
+    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + q0 + qq) * HD + static_cast<size_t>(h) * kD +
+                               8 * d8) = pack8<T>(num);
+  }
+  if (tid == 0) counters[unit] = 0;  // left zeroed for the next launch
+}
+
+// part [W, H, P, S, D+2] -> y [W, S, H*D]: one CTA per (window, head)
+template <typename T>
+__global__ void __launch_bounds__(128)
+    combine_kernel(const float *__restrict__ part, T *__restrict__ y, int S, int H, int P) {
+  const int wh = blockIdx.x;
+  const int w = wh / H, h = wh - w * H;
+  const size_t HD = static_cast<size_t>(H) * kD;
+  pdl_wait();
+  const float *base = part + static_cast<size_t>(wh) * P * S * (kD + 2);
+  for (int idx = threadIdx.x; idx < S * (kD / 8); idx += blockDim.x) {
+    const int s = idx / (kD / 8), d8 = idx - s * (kD / 8);
+    float top = kNegInf;
+    for (int i = 0; i < P; ++i) top = fmaxf(top, base[(i * S + s) * (kD + 2) + kD]);
+    float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
+    for (int i = 0; i < P; ++i) {
+      const float *ps = base + (i * S + s) * (kD + 2);
+      const float ms = ps[kD];
+      const float wgt = (ms == kNegInf) ? 0.f : exp2f(ms - top);  // slices without keys: weight 0
+      den = fmaf(wgt, ps[kD + 1], den);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) num[j] = fmaf(wgt, ps[8 * d8 + j], num[j]);
+    }
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) num[j] *= inv;
+    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + s) * HD + static_cast<size_t>(h) * kD + 8 * d8) =
+        pack8<T>(num);
+  }
+  pdl_launch_dependents();
+}
+
+int query_tiles(int S) {
+  const int nt = (S + 7) / 8;
+  return nt < 1 ? 1 : (nt > 4 ? 4 : nt);
+}
+
+// key slices of the fused kernel: about 8 CTAs per SM, at least 2 16-key blocks per warp
+int fused_splits(int W, int S, int H, int Tn) {
+  const int nt = query_tiles(S);
+  const long long units = static_cast<long long>(W) * H * ((S + nt * 8 - 1) / (nt * 8));
+  const long long target = 148LL * 8;
+  long long p = (target + units - 1) / units;
+  const long long blocks = (Tn + 15) / 16;
+  long long cap = blocks / (2 * kCrossWarps);
+  if (cap < 1) cap = 1;
+  if (p > cap) p = cap;
+  if (p < 1) p = 1;
+  return static_cast<int>(p);
+}
+
+size_t fused_workspace(int W, int S, int H, int Tn) {
+  const int nt = query_tiles(S);
+  const int qgs = (S + nt * 8 - 1) / (nt * 8);
+  const long long units = static_cast<long long>(W) * H * qgs;
+  const int P = fused_splits(W, S, H, Tn);
+  const size_t counters = (static_cast<size_t>(units) * sizeof(int) + 255) / 256 * 256;
+  return counters + static_cast<size_t>(units) * P * nt * 8 * (kD + 2) * sizeof(float);
+}
+
+float qk_scale() { return static_cast<float>(1.0 / sqrt(static_cast<double>(kD)) * 1.4426950408889634); }
+
+template <typename T, bool FUSED>
+int launch_cross(const void *q, const void *k, const void *v, float *part, int *counters, void *y, int W, int S,
+                 int H, int Tn, int P, void *stream) {
+  const int nt = query_tiles(S);
+  const int qgs = (S + nt * 8 - 1) / (nt * 8);
+  const dim3 grid(W * H, P, qgs), block(kCrossThreads);
+  const T *qq = static_cast<const T *>(q), *kk = static_cast<const T *>(k), *vv = static_cast<const T *>(v);
+  T *yy = static_cast<T *>(y);
+  const char *what = FUSED ? "cross_attn" : "cross_attn_split";
+  switch (nt) {
+    case 1: return launch(what, cross_kernel<T, 1, FUSED>, grid, block, 0, stream, qq, kk, vv, part, counters, yy, S, H, Tn, P, qk_scale());
+    case 2: return launch(what, cross_kernel<T, 2, FUSED>, grid, block, 0, stream, qq, kk, vv, part, counters, yy, S, H, Tn, P, qk_scale());
+    case 3: return launch(what, cross_kernel<T, 3, FUSED>, grid, block, 0, stream, qq, kk, vv, part, counters, yy, S, H, Tn, P, qk_scale());
+    default: return launch(what, cross_kernel<T, 4, FUSED>, grid, block, 0, stream, qq, kk, vv, part, counters, yy, S, H, Tn, P, qk_scale());
+  }
+}
+
+int check_cross(const char *what, int dtype, const void *q, const void *k, const void *v, const void *out, int W,
+                int S, int H, int Tn, int D) {
+  WT_REQUIRE(W > 0 && S > 0 && H > 0 && Tn > 0 && D > 0, WT_ERR_ARG,
+             "%s: sizes must be positive (windows %d, queries %d, heads %d, frames %d, head_dim %d)", what, W, S, H,
+             Tn, D);
+  WT_REQUIRE(q && k && v && out, WT_ERR_ARG, "%s: null pointer", what);
+  WT_ALIGNED(q);
+  WT_ALIGNED(k);
+  WT_ALIGNED(v);
+  WT_ALIGNED(out);
+  WT_REQUIRE(D == kD, WT_ERR_UNSUPPORTED, "%s: head_dim %d (this build: 64)", what, D);
+  WT_REQUIRE(dtype == WT_F16 || dtype == WT_BF16, WT_ERR_DTYPE, "%s: unknown dtype %d", what, dtype);
+  WT_REQUIRE(static_cast<long long>(W) * H < (1LL << 31), WT_ERR_ARG, "%s: windows*heads too large", what);
+  return WT_OK;
+}
+
+}  // namespace
+}  // namespace wt
+
+extern "C" {
+
+int wt_cross_attn_split(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
+                        int queries, int heads, int frames, int head_dim, int splits, void *stream) {
+  using namespace wt;
+  int st = check_cross("cross_attn_split", dtype, q, k, v, part, windows, queries, heads, frames, head_dim);
+  if (st != WT_OK) return st;
+  WT_REQUIRE(splits > 0 && splits <= 65535, WT_ERR_ARG, "cross_attn_split: splits %d", splits);
+  if (dtype == WT_F16)
+    return launch_cross<__half, false>(q, k, v, part, nullptr, nullptr, windows, queries, heads, frames, splits,
+                                       stream);
+  return launch_cross<__nv_bfloat16, false>(q, k, v, part, nullptr, nullptr, windows, queries, heads, frames,
+                                            splits, stream);
+}
+
+int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, int queries, int heads,
+                          int head_dim, int splits, void *stream) {
+  using namespace wt;
+  WT_REQUIRE(windows > 0 && queries > 0 && heads > 0 && splits > 0, WT_ERR_ARG,
+             "cross_attn_combine: sizes must be positive");
+  WT_REQUIRE(part && y, WT_ERR_ARG, "cross_attn_combine: null pointer");
+  WT_ALIGNED(part);
+  WT_ALIGNED(y);
+  WT_REQUIRE(head_dim == kD, WT_ERR_UNSUPPORTED, "cross_attn_combine: head_dim %d (this build: 64)", head_dim);
+  const dim3 grid(windows * heads), block(128);
+  if (dtype == WT_F16)
+    return launch("cross_attn_combine", combine_kernel<__half>, grid, block, 0, stream, part,
+                  static_cast<__half *>(y), queries, heads, splits);
+  if (dtype == WT_BF16)
+    return launch("cross_attn_combine", combine_kernel<__nv_bfloat16>, grid, block, 0, stream, part,
+                  static_cast<__nv_bfloat16 *>(y), queries, heads, splits);
+  return fail(WT_ERR_DTYPE, "cross_attn_combine: unknown dtype %d", dtype);
+}
+
+size_t wt_cross_attn_workspace(int windows, int queries, int heads, int frames, int head_dim) {
+  if (windows <= 0 || queries <= 0 || heads <= 0 || frames <= 0 || head_dim != wt::kD) return 0;
+  return wt::fused_workspace(windows, queries, heads, frames);
+}
+
+int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *y, int windows, int queries,
+                  int heads, int frames, int head_dim, void *workspace, size_t workspace_bytes, void *stream) {
+  using namespace wt;
+  int st = check_cross("cross_attn", dtype, q, k, v, y, windows, queries, heads, frames, head_dim);
+  if (st != WT_OK) return st;
+  const size_t need = fused_workspace(windows, queries, heads, frames);
+  WT_REQUIRE(workspace && workspace_bytes >= need, WT_ERR_WORKSPACE,
+             "cross_attn: needs a zeroed workspace of %zu bytes (given %zu)", need, workspace ? workspace_bytes : 0);
+  WT_ALIGNED(workspace);
+  const int nt = query_tiles(queries);
+  const long long units = static_cast<long long>(windows) * heads * ((queries + nt * 8 - 1) / (nt * 8));
+  int *counters = static_cast<int *>(workspace);
+  float *part = reinterpret_cast<float *>(static_cast<char *>(workspace) +
+                                          (static_cast<size_t>(units) * sizeof(int) + 255) / 256 * 256);
+  const int P = fused_splits(windows, queries, heads, frames);
+  if (dtype == WT_F16)
+    return launch_cross<__half, true>(q, k, v, part, counters, y, windows, queries, heads, frames, P, stream);
+  return launch_cross<__nv_bfloat16, true>(q, k, v, part, counters, y, windows, queries, heads, frames, P, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,114 @@
+"""Slot-table bookkeeping of beam search on the GPU (the step part that feeds parent indices to the attention).
+
+Beam search never moves the KV cache: row r (window r // K) reads each cache slot from the row ``src[r, slot]``
+names. Per step a new beam takes its parent's table and marks the slot its parent just wrote. These wrap the C-ABI
+kernels (``wt_beam_reorder``, ``wt_beam_update``, ``wt_slot_reset``); integer work, bit-exact with the reference:
+
+* :func:`beam_reorder` -- the reorder with the parents given: search.py:258 + :401-409 + :263-264;
+* :func:`update` -- a drop-in for the reference's ``beam_kernels.update(s, top_s, top_i, ns)``
+  (beam_kernels.py:292-302, kernel :169-269) in beam mode: CTranslate2's candidate rules, hypotheses, the new
+  beams' histories / tables / scores / tokens, prompt feeding, advancing;
+* :func:`slot_reset` -- a window loaded into slots (search.py:440-446).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(what: str, t: torch.Tensor, dtype: torch.dtype, shape: tuple | None = None) -> None:
+    if t.dtype != dtype:
+        raise TypeError(f"{what}: expected {dtype}, got {t.dtype}")
+    if not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{what}: contiguous CUDA tensors only")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{what}: expected shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def beam_reorder(src: torch.Tensor, parent: torch.Tensor, pos: torch.Tensor, hist: torch.Tensor | None = None,
+                 token: torch.Tensor | None = None, t: torch.Tensor | None = None, live: torch.Tensor | None = None,
+                 offset: torch.Tensor | None = None, advance: bool = True) -> None:
+    """In place: for each live window b and new beam k with parent p = parent[b, k], ``src[b*K+k] = src[b*K+p]``
+    with slot pos[b] marked as row b*K+p; ``hist`` likewise, with ``token`` written at t[b]; pos[b] += 1 when
+    ``advance``; ``offset`` (if given) = the rows' new pos. src [N, C] int32, parent [B, K] int64, pos [B] int64,
+    hist [N, T] int64, token [N] int64, t [B] int64, live [B] bool, offset [N] int64."""
+    what = "beam_reorder"
+    b, k = parent.shape
+    n, c = src.shape
+    if n != b * k:
+        raise ValueError(f"{what}: src has {n} rows, parent {b} x {k}")
+    _need(what, src, torch.int32)
+    _need(what, parent, torch.int64)
+    _need(what, pos, torch.int64, (b,))
+    tl = 0
+    if hist is not None:
+        _need(what, hist, torch.int64)
+        if hist.shape[0] != n:
+            raise ValueError(f"{what}: hist must have N rows")
+        tl = hist.shape[1]
+    if token is not None:
+        _need(what, token.view(-1), torch.int64, (n,))
+        if hist is None or t is None:
+            raise ValueError(f"{what}: token needs hist and t")
+    if t is not None:
+        _need(what, t, torch.int64, (b,))
+    if live is not None:
+        _need(what, live, torch.bool, (b,))
+    if offset is not None:
+        _need(what, offset, torch.int64, (n,))
+    dev = src.device
+    with torch.cuda.device(dev):
+        st = _lib.load().wt_beam_reorder(src.data_ptr(), _ptr(hist), _ptr(token), _ptr(t), parent.data_ptr(),
+                                         pos.data_ptr(), _ptr(live), _ptr(offset), b, k, c, tl, int(advance),
+                                         torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st, what)
+
+
+def update(s, top_s: torch.Tensor, top_i: torch.Tensor, ns: torch.Tensor) -> None:
+    """The step's bookkeeping on ``s`` (a search state with the reference Search's buffers, beam mode, no sampled
+    slots) from the best 2K candidates -- the reference's beam_kernels.update (beam_kernels.py:292-302)."""
+    what = "beam_update"
+    if getattr(s, "mixed", False):
+        raise ValueError(f"{what}: sampled slots (sampling_slots=True) are not supported by this kernel")
+    B, K = s.pos.shape[0], s.K
+    n, c = s.src.shape
+    T = s.hist.shape[1]
+    S = s.h_score.shape[1]
+    _need(what, top_s, torch.float32, (B, 2 * K))
+    _need(what, top_i, torch.int64, (B, 2 * K))
+    _need(what, ns, torch.float32, (B,))
+    for name, dt in (("t", torch.int64), ("pos", torch.int64), ("sot_pos", torch.int64), ("no_speech", torch.float32),
+                     ("done", torch.bool), ("hist", torch.int64), ("cum", torch.float32), ("src", torch.int32),
+                     ("tokens", torch.int64), ("forced", torch.int64), ("h_count", torch.int64),
+                     ("h_score", torch.float32), ("h_len", torch.int64), ("h_tokens", torch.int64),
+                     ("last_t", torch.int64)):
+        _need(f"{what}.{name}", getattr(s, name), dt)
+    dev = s.src.device
+    with torch.cuda.device(dev):
+        st = _lib.load().wt_beam_update(
+            top_s.data_ptr(), top_i.data_ptr(), s.t.data_ptr(), s.pos.data_ptr(), s.sot_pos.data_ptr(),
+            ns.data_ptr(), s.no_speech.data_ptr(), s.done.data_ptr(), s.hist.data_ptr(), s.cum.data_ptr(),
+            s.src.data_ptr(), s.tokens.data_ptr(), s.forced.data_ptr(), s.h_count.data_ptr(), s.h_score.data_ptr(),
+            s.h_len.data_ptr(), s.h_tokens.data_ptr(), s.last_t.data_ptr(), B, K, c, T, S, s.P, s.cfg.vocab_size,
+            s.cfg.eot, torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st, what)
+
+
+def slot_reset(src: torch.Tensor, slots: torch.Tensor, K: int, prefilled: bool) -> None:
+    """Rows of each slot s in ``slots`` read their own cache rows (src[r] = r) or, ``prefilled``, the slot's first
+    row (src[r] = s*K), as the reference's Search._start (search.py:440-446)."""
+    what = "slot_reset"
+    _need(what, src, torch.int32)
+    _need(what, slots, torch.int64)
+    n, c = src.shape
+    dev = src.device
+    with torch.cuda.device(dev):
+        st = _lib.load().wt_slot_reset(src.data_ptr(), slots.data_ptr(), slots.numel(), n // K, K, c, int(prefilled),
+                                       torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st, what)
