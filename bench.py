@@ -47,46 +47,63 @@ FALLBACK_HBM_GBS = 6650.0
 WORKLOADS = {
     # 8 slots x beam 5, 80 cached positions, random parent permutation every step
     "config2": dict(windows=8, beams=5, capacity=228, off_lo=80, off_hi=80, refill_p=0.0, advance=False,
-                    reorder="perm", desc="config 2: 8 slots x beam 5 = 40 rows, 80 cached positions (C = 228), "
+                    reorder="perm", refill_to=80, episode=0, desc="config 2: 8 slots x beam 5 = 40 rows, 80 cached positions (C = 228), "
                     "random parent permutation each step"),
     # 32 slots x beam 5, ragged U[4, 224], windows replaced (fresh length 4) with p = 0.02 per step
     "config3": dict(windows=32, beams=5, capacity=228, off_lo=4, off_hi=224, refill_p=0.02, advance=True,
-                    reorder="perm", desc="config 3: 32 slots x beam 5 = 160 rows, cache lengths U[4, 224] "
+                    reorder="perm", refill_to=4, episode=120, desc="config 3: 32 slots x beam 5 = 160 rows, cache lengths U[4, 224] "
                     "(C = 228), random parent reorder + append every step, windows replaced (fresh length 4) with "
                     "p = 0.02 per step"),
     # 16 slots x 5 samples, identity reorder, 224-token prompt prefix, lengths U[224, 447], C = 448
     "config4": dict(windows=16, beams=5, capacity=448, off_lo=224, off_hi=447, refill_p=0.0, advance=True,
-                    reorder="identity", desc="config 4: 16 slots x 5 samples = 80 rows, identity reorder, "
+                    reorder="identity", refill_to=224, episode=224, desc="config 4: 16 slots x 5 samples = 80 rows, identity reorder, "
                     "224-token prompt prefix, lengths U[224, 447] (C = 448)"),
     # 64 slots x beam 5 per GPU, U[4, 448], C = 448
     "config5": dict(windows=64, beams=5, capacity=448, off_lo=4, off_hi=447, refill_p=0.0, advance=True,
-                    reorder="perm", desc="config 5: 64 slots x beam 5 = 320 rows per GPU, cache lengths U[4, 448] "
+                    reorder="perm", refill_to=4, episode=200, desc="config 5: 64 slots x beam 5 = 320 rows per GPU, cache lengths U[4, 448] "
                     "(C = 448), random parent reorder every step"),
 }
 
 
 # --- the workload's schedule (host, deterministic) ------------------------------------------------------------
 class Schedule:
-    """Positions, parents and window replacements for ``n_steps`` steps of a workload (numpy, seeded)."""
+    """Positions, parents and window replacements for ``n_steps`` steps of a workload (numpy, seeded).
 
-    def __init__(self, wl: dict, n_steps: int, seed: int):
+    Windows start with cached lengths U[off_lo, off_hi]; every step each live window advances one position and its
+    beams take random parents (a permutation; identity for sampling); a window is replaced by a fresh one (length
+    ``refill_to``) with probability refill_p per step or when its cache is full. An episode (``episode`` steps,
+    counted from step ``start``, the first timed step) is the workload's run: at each episode start every window is
+    replaced by one with a fresh U[off_lo, off_hi] length, so any number of timed steps repeats the workload's
+    episode."""
+
+    def __init__(self, wl: dict, n_steps: int, seed: int, start: int = 0):
         rng = np.random.default_rng(seed)
         W, K, C = wl["windows"], wl["beams"], wl["capacity"]
         self.W, self.K, self.C, self.n = W, K, C, n_steps
-        pos = rng.integers(wl["off_lo"], wl["off_hi"] + 1, W).astype(np.int64)
+
+        def draw():
+            return rng.integers(wl["off_lo"], wl["off_hi"] + 1, W).astype(np.int64)
+
+        pos = draw()
         self.pos = np.zeros((n_steps + 1, W), dtype=np.int64)  # offsets used at step s
         self.refill = np.zeros((n_steps, W), dtype=bool)  # windows replaced after step s
+        self.refill_pos = np.zeros((n_steps, W), dtype=np.int64)  # ... with these lengths
         self.parent = np.zeros((n_steps, W, K), dtype=np.int64)
+        ep = wl["episode"]
         for s in range(n_steps):
             self.pos[s] = pos
             if wl["reorder"] == "perm":
                 self.parent[s] = np.stack([rng.permutation(K) for _ in range(W)])
             else:
                 self.parent[s] = np.arange(K)[None, :]
-            if wl["advance"]:
+            if ep and s + 1 >= start and (s + 1 - start) % ep == 0:
+                self.refill[s], self.refill_pos[s] = True, draw()
+            elif wl["advance"]:
                 fresh = (rng.random(W) < wl["refill_p"]) | (pos + 1 >= C)
                 self.refill[s] = fresh
-                pos = np.where(fresh, 4, pos + 1)
+                self.refill_pos[s] = wl["refill_to"]
+            if wl["advance"] or self.refill[s].any():
+                pos = np.where(self.refill[s], self.refill_pos[s], pos + (1 if wl["advance"] else 0))
         self.pos[n_steps] = pos
 
     def step_bytes(self, s: int, windows: slice | None = None) -> int:
@@ -191,7 +208,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     N = W * K
     n_sched = args.warmup + 2 * args.steps + 4
     seed = 1234 + 7919 * rank  # each rank its own windows (independent shards)
-    sch = Schedule(wl, n_sched, seed)
+    sch = Schedule(wl, n_sched, seed, start=args.warmup)
 
     g = torch.Generator(device=dev).manual_seed(seed)
     cache = torch.randn(L, 2, N, H, C, D, generator=g, device=dev, dtype=torch.float16)
@@ -207,6 +224,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     parents_all = torch.from_numpy(sch.parent).to(dev)
     refill_slots_all = torch.from_numpy(np.where(sch.refill, np.arange(W)[None, :], -1).astype(np.int64)).to(dev)
     refill_mask_all = torch.from_numpy(sch.refill).to(dev)
+    refill_pos_all = torch.from_numpy(sch.refill_pos).to(dev)
+    rpos_cur = torch.empty(1, W, dtype=torch.long, device=dev)
     live_all = ~refill_mask_all
     step_idx = torch.zeros(1, dtype=torch.long, device=dev)
     parent_cur = torch.empty(1, W, K, dtype=torch.long, device=dev)
@@ -222,8 +241,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         torch.index_select(refill_slots_all, 0, step_idx, out=slots_cur)
         torch.index_select(refill_mask_all, 0, step_idx, out=mask_cur)
         torch.index_select(live_all, 0, step_idx, out=live_cur)
+        torch.index_select(refill_pos_all, 0, step_idx, out=rpos_cur)
         sl.slot_reset(src, slots_cur.view(W), K, prefilled=False)
-        pos.masked_fill_(mask_cur.view(W), 4)
+        torch.where(mask_cur.view(W), rpos_cur.view(W), pos, out=pos)
         sl.beam_reorder(src, parent_cur.view(W, K), pos, live=live_cur.view(W), offset=offset,
                         advance=wl["advance"])
         step_idx.add_(1)
@@ -451,7 +471,7 @@ def run_cpu_baseline(wl: dict, sch: Schedule, min_seconds: float, sw: int) -> di
 def run_reference(args) -> dict:
     wl = WORKLOADS[args.workload]
     n_sched = args.warmup + args.steps + 4
-    sch = Schedule(wl, n_sched, 1234)
+    sch = Schedule(wl, n_sched, 1234, start=args.warmup)
     sw = min(wl["windows"], 2)
     smp = CpuSample(wl, sw, seed=99)
     for s in range(args.warmup):
@@ -482,7 +502,7 @@ def run_reference(args) -> dict:
 def main() -> None:
     ap_ = argparse.ArgumentParser()
     ap_.add_argument("--gpus", type=int, default=1)
-    ap_.add_argument("--steps", type=int, default=480)
+    ap_.add_argument("--steps", type=int, default=120)
     ap_.add_argument("--warmup", type=int, default=5)
     ap_.add_argument("--workload", default="config3", choices=sorted(WORKLOADS))
     ap_.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -518,7 +538,7 @@ def main() -> None:
         _lib.set_launch_flags(_lib.WT_LAUNCH_PDL)
     res = run_ours(args, rank, world, local_rank)
     if world == 1 and args.also:
-        also_args = argparse.Namespace(**{**vars(args), "workload": args.also, "steps": min(args.steps, 240)})
+        also_args = argparse.Namespace(**{**vars(args), "workload": args.also})
         torch.cuda.empty_cache()
         a = run_ours(also_args, rank, world, local_rank)
         res["also"] = {args.also: {k: a[k] for k in ("value", "unit", "ms_per_step", "us_per_step",
@@ -527,7 +547,8 @@ def main() -> None:
                           "bytes_per_step": a["config"]["bytes_per_step"]}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         wl = WORKLOADS[args.workload]
-        res["cpu_baseline"] = run_cpu_baseline(wl, Schedule(wl, 64, 1234), args.cpu_seconds,
+        res["cpu_baseline"] = run_cpu_baseline(wl, Schedule(wl, args.warmup + args.steps + 4, 1234, start=args.warmup),
+                                               args.cpu_seconds,
                                                min(wl["windows"], 2))
     elif rank == 0:
         res["cpu_baseline"] = {"value": None, "note": "timed on rank 0 at N=1 only"}
