@@ -94,6 +94,18 @@ int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, in
 size_t wt_cross_attn_workspace(int windows, int queries, int heads, int frames, int head_dim);
 int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *y, int windows, int queries,
                   int heads, int frames, int head_dim, void *workspace, size_t workspace_bytes, void *stream);
+/* wt_cross_attn_noalloc: no counterpart in the reference. The same cross-attention as wt_cross_attn for callers
+ *   that cannot allocate device memory while they run (a TensorRT-style plugin enqueue that must stay inside the
+ *   memory its engine planned; an application whose device memory belongs to its own allocator or budget): it takes
+ *   no workspace and allocates nothing. Its scratch is a fixed 8 MiB device array in this library (64 KiB of
+ *   counters + partials), which every GPU that loads the library holds until the process exits. Shapes needing
+ *   more (more than 16384 (window, head, query group) units, or partials above 8 MiB - 64 KiB -- e.g. more than
+ *   ~24 queries per window at 32 windows) are rejected with WT_ERR_UNSUPPORTED. The first call on a device looks up
+ *   the array's device address (cudaGetSymbolAddress); make that first call before any stream capture. Every call
+ *   shares the array and clears its counters (cudaMemsetAsync on `stream`) before the kernel: calls that overlap
+ *   on the GPU (other streams, other threads) race on it. */
+int wt_cross_attn_noalloc(int dtype, const void *q, const void *k, const void *v, void *y, int windows,
+                          int queries, int heads, int frames, int head_dim, void *stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * KV-cache append and gather (bit-exact copies).

@@ -473,3 +473,75 @@ int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *
 }
 
 }  // extern "C"
+
+// ---- wt_cross_attn_noalloc: the fused cross-attention with its scratch in a fixed device array -------------
+//
+// Some callers cannot allocate device memory while they run: a TensorRT-style plugin's enqueue has to work inside
+// the memory its engine planned ahead of time, and an application whose device memory is owned by its own
+// allocator (or that runs under a fixed memory budget) cannot let a library call cudaMalloc behind its back. For
+// them this variant of wt_cross_attn takes no workspace argument: the in-kernel combine's counters and partials
+// live in the array below, which every GPU that loads this library holds (8 MiB) until the process exits.
+
+// Layout: [0, 64 KiB) one int counter per (window, head, query group); [64 KiB, 8 MiB) the slices' partials.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+constexpr size_t kNoAllocCounterBytes = size_t(64) << 10;
+static __device__ __align__(256) unsigned char wt_cross_noalloc_scratch[kNoAllocScratchBytes];
+
+#include <mutex>
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// The device address of the scratch array on the current device, looked up once per device (the array's host-side
+// name is only a stand-in: kernels need this address).
+int noalloc_scratch(void **out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return wt::fail(WT_ERR_CUDA, "cross_attn_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return wt::fail(WT_ERR_UNSUPPORTED, "cross_attn_noalloc: device %d (at most %d devices)", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, wt_cross_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return wt::fail(WT_ERR_CUDA, "cross_attn_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                      cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return WT_OK;
+}
+
+}  // namespace
+
+extern "C" int wt_cross_attn_noalloc(int dtype, const void *q, const void *k, const void *v, void *y, int windows,
+                                     int queries, int heads, int frames, int head_dim, void *stream) {
+  using namespace wt;
+  int st = check_cross("cross_attn_noalloc", dtype, q, k, v, y, windows, queries, heads, frames, head_dim);
+  if (st != WT_OK) return st;
+  const int nt = query_tiles(queries);
+  const long long units = static_cast<long long>(windows) * heads * ((queries + nt * 8 - 1) / (nt * 8));
+  const int P = fused_splits(windows, queries, heads, frames);
+  const size_t counter_bytes = static_cast<size_t>(units) * sizeof(int);
+  const size_t part_bytes = static_cast<size_t>(units) * P * nt * 8 * (kD + 2) * sizeof(float);
+  WT_REQUIRE(counter_bytes <= kNoAllocCounterBytes && part_bytes <= kNoAllocScratchBytes - kNoAllocCounterBytes,
+             WT_ERR_UNSUPPORTED,
+             "cross_attn_noalloc: this shape needs %zu bytes of counters and %zu bytes of partials; the fixed "
+             "scratch holds %zu and %zu (use wt_cross_attn with a workspace)",
+             counter_bytes, part_bytes, kNoAllocCounterBytes, kNoAllocScratchBytes - kNoAllocCounterBytes);
+  void *base = nullptr;
+  st = noalloc_scratch(&base);
+  if (st != WT_OK) return st;
+  // the array keeps the previous call's contents: the counters must start at zero
+  cudaError_t e = cudaMemsetAsync(base, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(WT_ERR_CUDA, "cross_attn_noalloc: clearing the counters: %s", cudaGetErrorString(e));
+  int *counters = static_cast<int *>(base);
+  float *part = reinterpret_cast<float *>(static_cast<char *>(base) + kNoAllocCounterBytes);
+  if (dtype == WT_F16)
+    return launch_cross<__half, true>(q, k, v, part, counters, y, windows, queries, heads, frames, P, stream);
+  return launch_cross<__nv_bfloat16, true>(q, k, v, part, counters, y, windows, queries, heads, frames, P, stream);
+}

@@ -31,6 +31,8 @@ SIGNATURES = {
     "wt_cross_attn_workspace": (c_size, [c_int, c_int, c_int, c_int, c_int]),
     "wt_cross_attn": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void,
                               c_size, c_void]),
+    "wt_cross_attn_noalloc": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int,
+                                      c_void]),
     "wt_cache_append": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_void]),
     "wt_gather_cache": (c_int, [c_int, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_void]),
     "wt_beam_reorder": (c_int, [c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int,
