@@ -45,8 +45,14 @@ extern "C" {
 #define WT_ERR_WORKSPACE 5   /* workspace missing or smaller than the matching *_workspace() size */
 #define WT_ERR_CUDA 6        /* the CUDA launch failed */
 
-/* launch flags (wt_set_launch_flags) */
-#define WT_LAUNCH_PDL 1 /* programmatic dependent launch: a kernel may start while its predecessor drains */
+/* launch flags (wt_set_launch_flags)
+ * WT_LAUNCH_PDL: programmatic dependent launch. A kernel may start while the kernel launched just before it in the
+ *   same stream drains, and reads its predecessor-independent inputs before waiting for it: the self-attention
+ *   step its offsets, slot table and cache (slots below the offsets), the cross-attention its cross keys/values.
+ *   Those inputs must therefore not be written by the kernel launched immediately before (in a decoder step they
+ *   come from earlier steps and the encoder; the queries, which the preceding GEMM produces, are always read after
+ *   the wait). Every kernel waits for its predecessor before writing anything. */
+#define WT_LAUNCH_PDL 1
 
 int wt_abi_version(void);
 const char *wt_status_string(int status);
@@ -62,8 +68,9 @@ int wt_set_launch_flags(int flags);
  *   y [N, 1, H*D] (element type of qkv) = softmax(q k^T / sqrt(D)) v over [gathered cache | new token].
  *   write_cache != 0: the new key/value are also written into the row's own slot offset[r] (if < C) of
  *   k_cache / v_cache (rows only read slots below their offset, so the result does not change).
- *   kv_splits: 0 = choose from the shape; 1 = one CTA per (row, head); >1 = split every row's cache range over
- *   that many CTAs combined in-kernel, which needs `workspace` of wt_self_attn_step_workspace() bytes.
+ *   kv_splits: 0 = choose from the shape (wt_self_attn_step_splits); 1 = one warp per (row, head); >1 = split
+ *   every row's cache range into that many parts combined in-kernel, which needs `workspace` of
+ *   wt_self_attn_step_workspace() bytes. kv_splits must be at least ceil(capacity / 256).
  *   A workspace is laid out by the call's shape (rows, heads, head_dim, kv_splits): zero it before its first use
  *   with a shape; each call leaves its counters zeroed for the next call of the SAME shape (its partials stay as
  *   written, so another shape needs another -- or a re-zeroed -- workspace). Calls that may overlap on the GPU
@@ -86,6 +93,8 @@ int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, 
  *   launch (split + combine, the last CTA of each (window, head) combines); needs `workspace` of
  *   wt_cross_attn_workspace() bytes, with the same per-shape rule as wt_self_attn_step's: zeroed before its
  *   first use with a shape, valid for further calls of that shape only, not shared by calls that may overlap.
+ *   Its first 4 bytes are a device error word: non-zero after a kernel's bounded wait for its own TMA copies gave
+ *   up (the output is then not valid); the kernel never hangs. The size depends on the device's SM count.
  * ------------------------------------------------------------------------------------------------------- */
 int wt_cross_attn_split(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
                         int queries, int heads, int frames, int head_dim, int splits, void *stream);

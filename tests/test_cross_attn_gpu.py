@@ -156,3 +156,10 @@ def test_fused_alternating_shapes():
     for _ in range(2):
         for c, ref in zip(cases_, refs):
             assert_close(ap.cross_attn_triton(*c), ref)
+
+
+def test_no_device_errors_recorded():
+    """No kernel of the tests above gave up a bounded wait (the workspaces' device error words are zero)."""
+    q, k, v = rand_cross(2, 5, 20, 1500, torch.float16, seed=77)
+    ap.cross_attn_triton(q, k, v)
+    assert ap.workspace_errors() == 0

@@ -1,0 +1,197 @@
+"""Token parity on a random-init 32-layer whisper-large-v3-shaped decoder (fp16 weights N(0, 0.02), seeded).
+
+The same decoder step (whisper_trt_b200.decoder: the reference runtime.py:134-151 sequence, cuBLAS GEMMs) runs with
+its attention on this package's kernels and, as the reference, with the reference's attention op bodies
+(attn_plugin.py:92-136: slot-table gather, masked fp32 softmax, fp32 cross-attention) restated in torch fp32 on the
+GPU. Everything else -- weights, GEMMs, LayerNorms, the beam bookkeeping -- is shared, so the tokens can differ only
+through the attention outputs.
+
+* teacher-forced greedy decoding: the argmax token of every step is the same (the minimum top-1 margin of the
+  reference logits is reported);
+* teacher-forced beam search (beam 5, CTranslate2 rules through wt_beam_update driven by the reference's candidates):
+  the same best-K candidates at every step, except at near-ties whose reference score gap is within the measured
+  score difference (reported). A random-init decoder's distributions are nearly flat and repetitive, so free-running
+  beams can part at such a tie and never meet again; teacher forcing compares every step on the same state.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from whisper_trt_b200 import slots
+from whisper_trt_b200.decoder import Decoder, DecoderShape
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+SOT, EN, TRANSCRIBE, NO_TS, EOT = 50258, 50259, 50359, 50363, 50257
+PROMPT = [SOT, EN, TRANSCRIBE, NO_TS]
+
+
+def ref_self_attn_append(qkv, kc, vc, offset, src):
+    """attn_plugin.self_attn (reference body, :102-121) for one token, fp32, then the append at offset
+    (search.py:249-250)."""
+    b = qkv.shape[0]
+    h, c, d = kc.shape[1:]
+    off = offset.clamp(0, c)
+    rows = src.long().clamp(0, b - 1)
+    slot = torch.arange(c, device=qkv.device)
+    kg = kc.permute(0, 2, 1, 3)[rows, slot[None, :]].permute(0, 2, 1, 3).float()  # [B, H, C, D]
+    vg = vc.permute(0, 2, 1, 3)[rows, slot[None, :]].permute(0, 2, 1, 3).float()
+    q, k, v = qkv.view(b, 1, 3, h, d).permute(2, 0, 3, 1, 4).float().unbind(0)  # [B, H, 1, D]
+    keys, vals = torch.cat([kg, k], 2), torch.cat([vg, v], 2)
+    scores = (q * d**-0.5) @ keys.transpose(-1, -2)  # [B, H, 1, C+1]
+    ok = torch.cat([slot[None, :] < off[:, None], torch.ones(b, 1, dtype=torch.bool, device=qkv.device)], 1)
+    scores = scores.masked_fill(~ok[:, None, None, :], float("-inf"))
+    y = (scores.softmax(-1) @ vals).transpose(1, 2).reshape(b, 1, h * d).to(qkv.dtype)
+    idx = torch.arange(b, device=qkv.device)
+    w = off < c
+    kc[idx[w], :, off[w]] = k[w, :, 0].to(kc.dtype)
+    vc[idx[w], :, off[w]] = v[w, :, 0].to(vc.dtype)
+    return y
+
+
+def ref_cross_attn(q, k, v):
+    """attn_plugin.cross_attn (reference body, :129-136), fp32."""
+    w, s, _ = q.shape
+    h, d = k.shape[1], k.shape[3]
+    qh = q.view(w, s, h, d).transpose(1, 2).float()
+    p = ((qh * d**-0.5) @ k.float().transpose(-1, -2)).softmax(-1)
+    return (p @ v.float()).transpose(1, 2).reshape(w, s, h * d).to(q.dtype)
+
+
+@pytest.fixture(scope="module")
+def model():
+    torch.manual_seed(0)
+    dec = Decoder.random(DecoderShape(), seed=0)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    enc = torch.randn(4, 1500, 1280, generator=g, device="cuda", dtype=torch.float16)
+    return dec, dec.cross_kv(enc)
+
+
+def _buffers(dec, n, cap):
+    s = dec.shape
+    cache = torch.zeros(s.layers, 2, n, s.heads, cap, s.head_dim, dtype=torch.float16, device="cuda")
+    logits = torch.zeros(n, 1, s.vocab, dtype=torch.float32, device="cuda")
+    return cache, logits
+
+
+def test_teacher_forced_greedy_tokens_identical(model):
+    dec, cross = model
+    W, steps, cap = 4, 36, 48
+    src = torch.arange(W, dtype=torch.int32, device="cuda")[:, None].expand(W, cap).contiguous()
+    runs = {}
+    for name, sa, ca in (("ref", ref_self_attn_append, ref_cross_attn), ("b200", None, None)):
+        cache, logits = _buffers(dec, W, cap)
+        tokens = torch.zeros(W, 1, dtype=torch.long, device="cuda")
+        offset = torch.zeros(W, dtype=torch.long, device="cuda")
+        step = dec.step_fn(tokens, offset, cache, logits, None, src, cross, self_attn=sa, cross_attn=ca)
+        runs[name] = (tokens, offset, logits, step)
+    forced = []  # the reference's tokens, fed to both
+    mismatches, margins, max_diff = [], [], 0.0
+    for t in range(steps):
+        if t < len(PROMPT):
+            tok = torch.full((W,), PROMPT[t], dtype=torch.long, device="cuda")
+        else:
+            tok = forced[-1]
+        out = {}
+        for name, (tokens, offset, logits, step) in runs.items():
+            tokens[:, 0] = tok
+            offset.fill_(t)
+            step()
+            out[name] = logits[:, 0].clone()
+        ref, got = out["ref"], out["b200"]
+        max_diff = max(max_diff, float((ref - got).abs().max()))
+        top2 = ref.topk(2, dim=-1).values
+        margins.append(float((top2[:, 0] - top2[:, 1]).min()))
+        a_ref, a_got = ref.argmax(-1), got.argmax(-1)
+        if t >= len(PROMPT) - 1 and not torch.equal(a_ref, a_got):
+            mismatches.append((t, a_ref.tolist(), a_got.tolist(), margins[-1]))
+        forced.append(a_ref)
+    assert not mismatches, f"argmax differs at {mismatches} (max |logit diff| {max_diff:.3e})"
+    assert max_diff < 0.05, max_diff
+    print(f"greedy: {steps} steps x {W} windows identical; max |logit diff| {max_diff:.2e}; "
+          f"min top-1 margin {min(margins):.3e}")
+
+
+class _State:
+    """The reference Search's beam buffers (search.py:184-223) for B windows x K beams, prompts not prefilled,
+    loaded as Search._start does (search.py:421-464)."""
+
+    def __init__(self, B, K, P, cap, T, vocab, prompt):
+        dev = "cuda"
+        self.B, self.K, self.P = B, K, P
+        n = B * K
+        self.cfg = type("cfg", (), {"vocab_size": vocab, "eot": EOT})()
+        self.t = torch.full((B,), -(P - 1), dtype=torch.long, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.long, device=dev)
+        self.sot_pos = torch.zeros(B, dtype=torch.long, device=dev)
+        self.no_speech = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.done = torch.zeros(B, dtype=torch.bool, device=dev)
+        self.hist = torch.zeros(n, T, dtype=torch.long, device=dev)
+        self.cum = torch.tensor([0.0 if k == 0 else float("-inf") for _ in range(B) for k in range(K)],
+                                dtype=torch.float32, device=dev)
+        self.src = torch.arange(n, dtype=torch.int32, device=dev)[:, None].expand(n, cap).contiguous()
+        self.tokens = torch.full((n,), prompt[0], dtype=torch.long, device=dev)
+        self.forced = torch.tensor([prompt + [0]] * B, dtype=torch.long, device=dev)
+        S = 2 * K + 1
+        self.h_count = torch.zeros(B, dtype=torch.long, device=dev)
+        self.h_score = torch.full((B, S), float("-inf"), dtype=torch.float32, device=dev)
+        self.h_len = torch.zeros(B, S, dtype=torch.long, device=dev)
+        self.h_tokens = torch.zeros(B, S, T, dtype=torch.long, device=dev)
+        self.last_t = torch.full((B,), T - 1, dtype=torch.long, device=dev)
+
+
+def test_teacher_forced_beam_candidates_identical(model):
+    """Beam search (beam 5, 2 windows) teacher-forced: both attention paths score the same states, the reference's
+    best 2K candidates drive the (shared) bookkeeping through wt_beam_update, and each step's best-K candidate sets
+    must agree -- except where the reference's own gap between the candidates that swapped is within the measured
+    score difference (a near-tie; counted and reported)."""
+    dec, cross = model
+    B, K, T = 2, 5, 24
+    P, cap = len(PROMPT), len(PROMPT) + T + 2
+    V = dec.shape.vocab
+    cross2 = cross[:, :, :B].contiguous()
+    st = _State(B, K, P, cap, T, V, PROMPT)
+    tokens = st.tokens.view(-1, 1)
+    offset = torch.zeros(B * K, dtype=torch.long, device="cuda")
+    runs = {}
+    for name, sa, ca in (("ref", ref_self_attn_append, ref_cross_attn), ("b200", None, None)):
+        cache, logits = _buffers(dec, B * K, cap)
+        runs[name] = (logits, dec.step_fn(tokens, offset, cache, logits, None, st.src, cross2, self_attn=sa,
+                                          cross_attn=ca))
+    beam_steps, exact, near_ties, worst = 0, 0, [], 0.0
+    for _ in range(P - 1 + T):
+        if bool(st.done.all()):
+            break
+        offset.copy_(st.pos.repeat_interleave(K))
+        in_prompt = bool((st.t < 0).all())
+        scored = {}
+        for name, (logits, step) in runs.items():
+            step()
+            logp = logits[:, 0].log_softmax(-1)
+            first = (st.t == 0).repeat_interleave(K)[:, None]
+            logp = torch.where(first & (torch.arange(V, device="cuda") == EOT), torch.finfo(torch.float32).min,
+                               logp)
+            scored[name] = (logp + st.cum[:, None]).view(B, K * V)
+        ref_s, ref_i = scored["ref"].topk(2 * K, dim=1)
+        if not in_prompt:
+            beam_steps += 1
+            _, got_i = scored["b200"].topk(K, dim=1)
+            diff = float((scored["ref"] - scored["b200"]).abs()[torch.isfinite(scored["ref"])].max())
+            worst = max(worst, diff)
+            for b in range(B):
+                a, g = set(ref_i[b, :K].tolist()), set(got_i[b].tolist())
+                if a == g:
+                    exact += 1
+                    continue
+                # the swapped candidates' reference scores: a near-tie iff their gap is within the error
+                sw = [scored["ref"][b, i].item() for i in (a ^ g)]
+                gap = max(sw) - min(sw)
+                near_ties.append((b, gap, diff))
+                assert gap <= 4 * diff, f"window {b}: candidates differ by {gap:.3e} >> score error {diff:.3e}"
+        lg = runs["ref"][0][::K, 0]
+        ns = (lg[:, 0] - lg.logsumexp(-1)).exp()
+        slots.update(st, ref_s.contiguous(), ref_i.contiguous(), ns.contiguous())
+    assert beam_steps >= 10
+    print(f"beam: {exact} of {beam_steps * B} window-steps with identical best-{K} candidates; near-ties "
+          f"{[(b, f'{g:.1e}') for b, g, _ in near_ties]}; max |score diff| {worst:.2e}")

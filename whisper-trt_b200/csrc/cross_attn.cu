@@ -19,137 +19,19 @@
 //     for bf16 inputs P is split into hi + lo bf16 parts (two mma) to keep ~16 bits of it.
 // One CTA of 4 warps per (window, head, key slice, query group); each warp streams 16-key blocks of the slice
 // with the next block's loads in flight while the current one is computed.
-#include <type_traits>
-
-#include "common.cuh"
+#include "cross_math.cuh"
 
 namespace wt {
+
+// the fused kernel (cross_stream.cu)
+size_t cross_stream_workspace(int W, int S, int H, int Tn);
+int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y, int W, int S, int H, int Tn,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
 namespace {
 
 constexpr int kCrossWarps = 4;
 constexpr int kCrossThreads = kCrossWarps * 32;
-constexpr int kD = 64;
-
-template <typename T> struct Mma;
-template <> struct Mma<__half> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-};
-template <> struct Mma<__nv_bfloat16> {
-  static __device__ __forceinline__ void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-};
-
-__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
-  uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-// The operands of one 16-key block for one lane (g = lane / 4, c = lane % 4):
-//   ka/kb: key rows g and g+8, head-dim pieces [8c, 8c+8) and [32+8c, 32+8c+8)
-//   v0..v3: value rows 2c, 2c+1, 2c+8, 2c+9, head-dim piece [8g, 8g+8)
-struct Block {
-  uint4 ka0, kb0, ka1, kb1, v0, v1, v2, v3;
-};
-
-template <typename T>
-__device__ __forceinline__ void load_block(Block &b, const T *kb, const T *vb, int k0, int hi, int g, int c) {
-  const int last = hi - 1;
-  const int r0 = min(k0 + g, last), r8 = min(k0 + g + 8, last);
-  b.ka0 = ldg_stream(kb + static_cast<size_t>(r0) * kD + 8 * c);
-  b.kb0 = ldg_stream(kb + static_cast<size_t>(r0) * kD + 32 + 8 * c);
-  b.ka1 = ldg_stream(kb + static_cast<size_t>(r8) * kD + 8 * c);
-  b.kb1 = ldg_stream(kb + static_cast<size_t>(r8) * kD + 32 + 8 * c);
-  b.v0 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c, last)) * kD + 8 * g);
-  b.v1 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c + 1, last)) * kD + 8 * g);
-  b.v2 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c + 8, last)) * kD + 8 * g);
-  b.v3 = ldg_stream(vb + static_cast<size_t>(min(k0 + 2 * c + 9, last)) * kD + 8 * g);
-}
-
-template <int NT>
-struct State {
-  float m[NT][2], l[NT][2], o[NT][4][4];
-};
-
-template <typename T, int NT>
-__device__ __forceinline__ void compute_block(State<NT> &st, const Block &b, const uint32_t (&qf)[NT][8], int k0,
-                                              int hi, int g, float scale) {
-  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
-  const bool ok0 = (k0 + g) < hi, ok8 = (k0 + g + 8) < hi;
-  // V^T operand fragments for the 4 head-dim tiles (shared by all query tiles)
-  uint32_t va[4][4];
-  const uint32_t w0[4] = {b.v0.x, b.v0.y, b.v0.z, b.v0.w}, w1[4] = {b.v1.x, b.v1.y, b.v1.z, b.v1.w};
-  const uint32_t w2[4] = {b.v2.x, b.v2.y, b.v2.z, b.v2.w}, w3[4] = {b.v3.x, b.v3.y, b.v3.z, b.v3.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    va[i][0] = __byte_perm(w0[i], w1[i], 0x5410);
-    va[i][1] = __byte_perm(w0[i], w1[i], 0x7632);
-    va[i][2] = __byte_perm(w2[i], w3[i], 0x5410);
-    va[i][3] = __byte_perm(w2[i], w3[i], 0x7632);
-  }
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-    Mma<T>::run(sc, b.ka0.x, b.ka1.x, b.ka0.y, b.ka1.y, qf[nt][0], qf[nt][1]);
-    Mma<T>::run(sc, b.ka0.z, b.ka1.z, b.ka0.w, b.ka1.w, qf[nt][2], qf[nt][3]);
-    Mma<T>::run(sc, b.kb0.x, b.kb1.x, b.kb0.y, b.kb1.y, qf[nt][4], qf[nt][5]);
-    Mma<T>::run(sc, b.kb0.z, b.kb1.z, b.kb0.w, b.kb1.w, qf[nt][6], qf[nt][7]);
-    // sc: (key g, query 2c), (key g, query 2c+1), (key g+8, query 2c), (key g+8, query 2c+1)
-    const float s0 = ok0 ? sc[0] * scale : kNegInf, s1 = ok0 ? sc[1] * scale : kNegInf;
-    const float s2 = ok8 ? sc[2] * scale : kNegInf, s3 = ok8 ? sc[3] * scale : kNegInf;
-    float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    const float mn0 = fmaxf(st.m[nt][0], mx0), mn1 = fmaxf(st.m[nt][1], mx1);  // finite: k0 < hi
-    const float a0 = exp2f(st.m[nt][0] - mn0), a1 = exp2f(st.m[nt][1] - mn1);
-    st.m[nt][0] = mn0;
-    st.m[nt][1] = mn1;
-    const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1), p2 = exp2f(s2 - mn0), p3 = exp2f(s3 - mn1);
-    const uint32_t h01 = Elem<T>::from_float2(p0, p1), h23 = Elem<T>::from_float2(p2, p3);
-    const float2 r01 = Elem<T>::to_float2(h01), r23 = Elem<T>::to_float2(h23);
-    float l0 = r01.x + r23.x, l1 = r01.y + r23.y;
-    uint32_t lo01 = 0, lo23 = 0;
-    if (kSplitP) {
-      lo01 = Elem<T>::from_float2(p0 - r01.x, p1 - r01.y);
-      lo23 = Elem<T>::from_float2(p2 - r23.x, p3 - r23.y);
-      const float2 q01 = Elem<T>::to_float2(lo01), q23 = Elem<T>::to_float2(lo23);
-      l0 += q01.x + q23.x;
-      l1 += q01.y + q23.y;
-    }
-    st.l[nt][0] = st.l[nt][0] * a0 + l0;
-    st.l[nt][1] = st.l[nt][1] * a1 + l1;
-    const uint32_t pb0 = movmatrix_trans(h01), pb1 = movmatrix_trans(h23);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      st.o[nt][i][0] *= a0;
-      st.o[nt][i][1] *= a1;
-      st.o[nt][i][2] *= a0;
-      st.o[nt][i][3] *= a1;
-      Mma<T>::run(st.o[nt][i], va[i][0], va[i][1], va[i][2], va[i][3], pb0, pb1);
-    }
-    if (kSplitP) {
-      const uint32_t qb0 = movmatrix_trans(lo01), qb1 = movmatrix_trans(lo23);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) Mma<T>::run(st.o[nt][i], va[i][0], va[i][1], va[i][2], va[i][3], qb0, qb1);
-    }
-  }
-}
 
 // Shared-memory layout of the CTA reduction: per warp, NT*8 queries x (64 outputs, m, l).
 template <int NT>
@@ -449,7 +331,7 @@ int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, in
 
 size_t wt_cross_attn_workspace(int windows, int queries, int heads, int frames, int head_dim) {
   if (windows <= 0 || queries <= 0 || heads <= 0 || frames <= 0 || head_dim != wt::kD) return 0;
-  return wt::fused_workspace(windows, queries, heads, frames);
+  return wt::cross_stream_workspace(windows, queries, heads, frames);
 }
 
 int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *y, int windows, int queries,
@@ -457,19 +339,8 @@ int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *
   using namespace wt;
   int st = check_cross("cross_attn", dtype, q, k, v, y, windows, queries, heads, frames, head_dim);
   if (st != WT_OK) return st;
-  const size_t need = fused_workspace(windows, queries, heads, frames);
-  WT_REQUIRE(workspace && workspace_bytes >= need, WT_ERR_WORKSPACE,
-             "cross_attn: needs a zeroed workspace of %zu bytes (given %zu)", need, workspace ? workspace_bytes : 0);
-  WT_ALIGNED(workspace);
-  const int nt = query_tiles(queries);
-  const long long units = static_cast<long long>(windows) * heads * ((queries + nt * 8 - 1) / (nt * 8));
-  int *counters = static_cast<int *>(workspace);
-  float *part = reinterpret_cast<float *>(static_cast<char *>(workspace) +
-                                          (static_cast<size_t>(units) * sizeof(int) + 255) / 256 * 256);
-  const int P = fused_splits(windows, queries, heads, frames);
-  if (dtype == WT_F16)
-    return launch_cross<__half, true>(q, k, v, part, counters, y, windows, queries, heads, frames, P, stream);
-  return launch_cross<__nv_bfloat16, true>(q, k, v, part, counters, y, windows, queries, heads, frames, P, stream);
+  if (workspace) WT_ALIGNED(workspace);
+  return cross_stream(dtype, q, k, v, y, windows, queries, heads, frames, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

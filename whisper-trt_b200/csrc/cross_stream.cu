@@ -1,0 +1,390 @@
+// Fused cross-attention (split + combine in one launch) as a persistent, stream-K balanced kernel fed by TMA.
+//
+// Semantics: the reference's cross_attn (attn_plugin.py:129-136, kernel :352-376) -- softmax(q k^T / sqrt(D)) v per
+// (window, head) over the window's T encoder frames, scores in log2 units; fp32 accumulation.
+//
+// B200 design. The work is the flat sequence of (window, head, query group, 16-key block) units -- 94 blocks per
+// (window, head) at T = 1500 -- cut into one equal contiguous range per warp of a grid of one CTA per SM
+// ("stream-K": every warp streams the same number of bytes, no wave tail whatever the window count):
+//   * each warp owns a ring of 4 stages in shared memory; its lane 0 issues 2D TMA loads (16 rows x 128 bytes of K and
+//     of V, 128-byte swizzle) that complete on the stage's mbarrier, keeping three blocks in flight while the warp
+//     computes the fourth -- no registers are held by loads in flight;
+//   * the block's mma operands are read from the swizzled tile with bank-conflict-free 16-byte shared loads and
+//     go through the same tensor-core math as the split kernel (cross_math.cuh);
+//   * when a warp's range crosses into the next (window, head), it writes its partial (acc, m, l) for the finished
+//     one; the warp that completes a (window, head) -- an atomic count of its blocks, no waiting -- combines the
+//     partials (at most ceil(94 / blocks per warp) + 1 of them) and writes the output.
+// Every mbarrier wait is bounded: a wait that times out records an error code in the workspace and the warp goes on.
+// With programmatic dependent launch the first TMA loads are issued before the preceding kernel has finished (the
+// cross keys/values are not its output); the queries are read after it, one unit ahead of their use.
+#include <cstdlib>
+
+#include "cross_math.cuh"
+#include "tma.cuh"
+
+namespace wt {
+namespace {
+
+constexpr int kTileBytes = 16 * 128;         // 16 keys x 64 elements x 2 bytes
+constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
+constexpr int kErrTimeout = 1;
+
+// Launch shapes: warps per CTA (one CTA per SM) x ring stages per warp. Shared memory: warps * stages * 4 KB.
+struct Shape {
+  int warps, stages;
+  bool pair;  // two 16-key blocks per step of the online softmax
+};
+constexpr Shape kShapes[] = {{12, 4, false}, {12, 4, true}, {8, 6, true}, {10, 5, true}, {16, 3, false}};
+
+constexpr int smem_bytes(int warps, int stages) { return warps * stages * kStageBytes + warps * stages * 8 + 1024; }
+
+struct StreamArgs {
+  const void *q;
+  void *y;
+  float *part;
+  int *counters;
+  int *err;
+  int W, S, H, Tn, QG, bpu;
+  long long total;
+  long long per_warp;
+  int max_slots;
+  float scale;
+};
+
+__host__ __device__ inline long long first_warp(long long u, int bpu, long long per_warp) {
+  return u * bpu / per_warp;
+}
+__host__ __device__ inline long long last_warp(long long u, int bpu, long long per_warp) {
+  return ((u + 1) * bpu - 1) / per_warp;
+}
+
+template <int NT>
+__device__ __forceinline__ void reset_state(State<NT> &st) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    st.m[nt][0] = st.m[nt][1] = kNegInf;
+    st.l[nt][0] = st.l[nt][1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.o[nt][i][j] = 0.f;
+  }
+}
+
+// The warp's partial for unit u (its `nblk` blocks of it) -> workspace; the warp that completes u combines.
+template <typename T, int NT>
+__device__ void flush_unit(State<NT> &st, const StreamArgs &a, long long u, int nblk, long long gw, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) st.l[nt][j] += __shfl_xor_sync(0xffffffffu, st.l[nt][j], o);
+  const long long fw = first_warp(u, a.bpu, a.per_warp);
+  const int slot = static_cast<int>(gw - fw);
+  float *dst = a.part + (static_cast<size_t>(u) * a.max_slots + slot) * (NT * 8) * (kD + 2);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float *rq = dst + (nt * 8 + 2 * c + j) * (kD + 2);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        rq[16 * i + g] = st.o[nt][i][j];
+        rq[16 * i + g + 8] = st.o[nt][i][j + 2];
+      }
+      if (g == 0) {
+        rq[kD] = st.m[nt][j];
+        rq[kD + 1] = st.l[nt][j];
+      }
+    }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = (atomicAdd(a.counters + u, nblk) + nblk == a.bpu);
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  const int nslots = static_cast<int>(last_warp(u, a.bpu, a.per_warp) - fw + 1);
+  const int wh = static_cast<int>(u / a.QG), qg = static_cast<int>(u % a.QG);
+  const int w = wh / a.H, h = wh - w * a.H;
+  const int q0 = qg * NT * 8;
+  const int nq = min(NT * 8, a.S - q0);
+  const float *base = a.part + static_cast<size_t>(u) * a.max_slots * (NT * 8) * (kD + 2);
+  const size_t HD = static_cast<size_t>(a.H) * kD;
+  T *y = static_cast<T *>(a.y);
+  for (int idx = lane; idx < nq * (kD / 8); idx += 32) {
+    const int qq = idx / (kD / 8), d8 = idx - qq * (kD / 8);
+    float top = kNegInf;
+    for (int s2 = 0; s2 < nslots; ++s2) top = fmaxf(top, __ldcg(base + (s2 * NT * 8 + qq) * (kD + 2) + kD));
+    float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
+    for (int s2 = 0; s2 < nslots; ++s2) {
+      const float *ps = base + (s2 * NT * 8 + qq) * (kD + 2);
+      const float ms = __ldcg(ps + kD);
+      const float wgt = (ms == kNegInf) ? 0.f : exp2f(ms - top);
+      den = fmaf(wgt, __ldcg(ps + kD + 1), den);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(ps + 8 * d8 + i), num[i]);
+    }
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) num[i] *= inv;
+    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * a.S + q0 + qq) * HD + static_cast<size_t>(h) * kD +
+                               8 * d8) = pack8<T>(num);
+  }
+  if (lane == 0) a.counters[u] = 0;  // left zeroed for the next launch
+}
+
+template <typename T, int NT, int kStreamWarps, int kStreamStages, bool kPair>
+__global__ void __launch_bounds__(kStreamWarps * 32, 1)
+    cross_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        const StreamArgs a) {
+  constexpr int kWarpRing = kStreamStages * kStageBytes;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  unsigned char *ring = smem + warp * kWarpRing;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStreamWarps * kWarpRing) + warp * kStreamStages;
+  const long long gw = static_cast<long long>(blockIdx.x) * kStreamWarps + warp;
+  const long long beg = gw * a.per_warp;
+  const long long end = min(beg + a.per_warp, a.total);
+  if (lane == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+#pragma unroll
+    for (int s = 0; s < kStreamStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const int n = beg < end ? static_cast<int>(end - beg) : 0;
+
+  // the range's position as (window-head, query group, block), advanced without divisions
+  const long long u0 = n ? beg / a.bpu : 0;
+  int i_wh = static_cast<int>(u0 / a.QG), i_qg = static_cast<int>(u0 % a.QG);
+  int i_b = static_cast<int>(beg - u0 * a.bpu);
+  int issued = 0;
+  auto issue_next = [&]() {  // lane 0: the next block of the range into its stage
+    const int s = issued % kStreamStages;
+    unsigned char *dst = ring + s * kStageBytes;
+    const int row = i_wh * a.Tn + i_b * 16;
+    mbar_arrive_expect_tx(&bars[s], kStageBytes);
+    tma_load_2d(dst, &kmap, 0, row, &bars[s]);
+    tma_load_2d(dst + kTileBytes, &vmap, 0, row, &bars[s]);
+    ++issued;
+    if (++i_b == a.bpu) {
+      i_b = 0;
+      if (++i_qg == a.QG) {
+        i_qg = 0;
+        ++i_wh;
+      }
+    }
+  };
+  if (lane == 0)
+    while (issued < min(n, kStreamStages)) issue_next();
+  // (everything above reads only the cross keys/values, which the kernel launched just before this one does not
+  // write; the queries, the workspace and the output wait for it)
+  pdl_wait();
+
+  const T *q = static_cast<const T *>(a.q);
+  const size_t HD = static_cast<size_t>(a.H) * kD;
+  uint32_t qf[NT][8], qn[NT][8];  // this unit's query fragments, and the next unit's, loaded one unit ahead
+  State<NT> st;
+  long long cur = -1;
+  int nblk = 0;
+  uint32_t late = 0;  // stages whose wait timed out (their copies may still be in flight)
+  int c_wh = static_cast<int>(u0 / a.QG), c_qg = static_cast<int>(u0 % a.QG);
+  int c_b = static_cast<int>(beg - u0 * a.bpu);
+  long long c_u = u0;
+  for (int j = 0; j < n;) {
+    if (c_u != cur) {
+      if (cur >= 0) {
+        flush_unit<T, NT>(st, a, cur, nblk, gw, lane);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) qf[nt][i] = qn[nt][i];
+      } else {
+        const int w = c_wh / a.H, h = c_wh - w * a.H;
+        load_q_std<T, NT>(qf, q + static_cast<size_t>(w) * a.S * HD + static_cast<size_t>(h) * kD, HD,
+                          c_qg * NT * 8, a.S, g, c);
+      }
+      cur = c_u;
+      nblk = 0;
+      reset_state<NT>(st);
+      // the next unit's queries, needed only after this unit's blocks of the range
+      int n_wh = c_wh, n_qg = c_qg + 1;
+      if (n_qg == a.QG) {
+        n_qg = 0;
+        ++n_wh;
+      }
+      if (n_wh < a.W * a.H) {
+        const int w = n_wh / a.H, h = n_wh - w * a.H;
+        load_q_std<T, NT>(qn, q + static_cast<size_t>(w) * a.S * HD + static_cast<size_t>(h) * kD, HD,
+                          n_qg * NT * 8, a.S, g, c);
+      }
+    }
+    // two blocks at once when the range's next block belongs to the same (window, head)
+    const bool pair = kPair && j + 1 < n && c_b + 1 < a.bpu;
+    const int s0 = j % kStreamStages;
+    if (!mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kStreamStages) & 1), a.err, kErrTimeout))
+      late |= 1u << s0;
+    uint32_t ka[4][4], va[4][4];
+    smem_frags(ka, va, ring + s0 * kStageBytes, ring + s0 * kStageBytes + kTileBytes, lane);
+    const int k0 = c_b * 16;
+    const int used = pair ? 2 : 1;
+    if (pair) {
+      const int s1 = (j + 1) % kStreamStages;
+      if (!mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kStreamStages) & 1), a.err, kErrTimeout))
+        late |= 1u << s1;
+      uint32_t kb[4][4], vb[4][4];
+      smem_frags(kb, vb, ring + s1 * kStageBytes, ring + s1 * kStageBytes + kTileBytes, lane);
+      // the stages' operands are in registers (their shared-memory reads are complete): refill the stages now,
+      // so every stage of the ring is in flight while this warp computes
+      consume_frags(ka, va);
+      consume_frags(kb, vb);
+      __syncwarp();
+      if (lane == 0)
+        for (int u = 0; u < used && issued < n; ++u) issue_next();
+      const bool ok[2][2] = {{k0 + g < a.Tn, k0 + g + 8 < a.Tn}, {k0 + 16 + g < a.Tn, k0 + 24 + g < a.Tn}};
+      attend_block2<T, NT>(st, ka, va, kb, vb, qf, ok, a.scale);
+    } else {
+      consume_frags(ka, va);
+      __syncwarp();
+      if (lane == 0 && issued < n) issue_next();
+      attend_block<T, NT>(st, ka, va, qf, k0 + g < a.Tn, k0 + g + 8 < a.Tn, a.scale);
+    }
+    nblk += used;
+    j += used;
+    c_b += used;
+    if (c_b == a.bpu) {
+      c_b = 0;
+      ++c_u;
+      if (++c_qg == a.QG) {
+        c_qg = 0;
+        ++c_wh;
+      }
+    }
+  }
+  if (cur >= 0) flush_unit<T, NT>(st, a, cur, nblk, gw, lane);
+  // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
+  for (int j = n - min(n, kStreamStages); j < n; ++j) {
+    const int s = j % kStreamStages;
+    if (late & (1u << s)) mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kStreamStages) & 1), nullptr, 0);
+  }
+  pdl_launch_dependents();
+}
+
+int g_sm_count[64] = {};
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+// The launch shape: kShapes[WT_CROSS_SHAPE] if that environment variable is set (a tuning knob), else the default.
+int shape_index() {
+  static int idx = -1;
+  if (idx < 0) {
+    const char *e = getenv("WT_CROSS_SHAPE");
+    int v = e ? atoi(e) : 1;
+    idx = (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : 1;
+  }
+  return idx;
+}
+
+struct StreamPlan {
+  int nt, qgs, bpu, max_slots, grid, shape;
+  long long units, total, per_warp;
+  size_t counters_off, part_off, bytes;
+};
+
+StreamPlan plan_stream(int W, int S, int H, int Tn) {
+  StreamPlan p{};
+  p.nt = (S + 7) / 8 > 4 ? 4 : (S + 7) / 8;
+  p.qgs = (S + p.nt * 8 - 1) / (p.nt * 8);
+  p.bpu = (Tn + 15) / 16;
+  p.units = static_cast<long long>(W) * H * p.qgs;
+  p.total = p.units * p.bpu;
+  p.grid = sm_count();
+  p.shape = p.nt >= 2 ? 0 : shape_index();  // (more query tiles: one block per step keeps them in registers)
+  const long long warps = static_cast<long long>(p.grid) * kShapes[p.shape].warps;
+  p.per_warp = (p.total + warps - 1) / warps;
+  p.max_slots = static_cast<int>((p.bpu + p.per_warp - 1) / p.per_warp + 1);
+  p.counters_off = 256;  // [0, 256): the device error word
+  p.part_off = p.counters_off + (static_cast<size_t>(p.units) * sizeof(int) + 255) / 256 * 256;
+  p.bytes = p.part_off + static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * (kD + 2) * sizeof(float);
+  return p;
+}
+
+template <typename T, int NT, int WARPS, int STAGES, bool PAIR>
+int launch_stream_shape(const CUtensorMap &km, const CUtensorMap &vm, const StreamArgs &a, int grid, void *stream) {
+  constexpr int smem = smem_bytes(WARPS, STAGES);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(cross_stream_kernel<T, NT, WARPS, STAGES, PAIR>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  return launch("cross_attn", cross_stream_kernel<T, NT, WARPS, STAGES, PAIR>, dim3(grid), dim3(WARPS * 32), smem,
+                stream, km, vm, a);
+}
+
+template <typename T, int NT>
+int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamArgs &a, int grid, int shape,
+                     void *stream) {
+  switch (shape) {
+#define WT_SHAPE_CASE(i)                                                                                      \
+  case i:                                                                                                    \
+    return launch_stream_shape<T, NT, kShapes[i].warps, kShapes[i].stages, kShapes[i].pair>(km, vm, a, grid, \
+                                                                                             stream);
+    WT_SHAPE_CASE(0)
+    WT_SHAPE_CASE(1)
+    WT_SHAPE_CASE(2)
+    WT_SHAPE_CASE(3)
+    default:
+      return launch_stream_shape<T, NT, kShapes[4].warps, kShapes[4].stages, kShapes[4].pair>(km, vm, a, grid,
+                                                                                             stream);
+#undef WT_SHAPE_CASE
+  }
+}
+
+}  // namespace
+
+size_t cross_stream_workspace(int W, int S, int H, int Tn) { return plan_stream(W, S, H, Tn).bytes; }
+
+int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y, int W, int S, int H, int Tn,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+  const StreamPlan p = plan_stream(W, S, H, Tn);
+  WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,
+             "cross_attn: needs a zeroed workspace of %zu bytes (given %zu)", p.bytes, workspace ? workspace_bytes : 0);
+  WT_REQUIRE(p.total < (1LL << 40), WT_ERR_ARG, "cross_attn: too large");
+  CUtensorMap km, vm;
+  const unsigned long long rows = static_cast<unsigned long long>(W) * H * Tn;
+  int st = encode_rows128_map(&km, k, rows, 16, dtype);
+  if (st != WT_OK) return st;
+  st = encode_rows128_map(&vm, v, rows, 16, dtype);
+  if (st != WT_OK) return st;
+  char *ws = static_cast<char *>(workspace);
+  StreamArgs a{q,       y,    reinterpret_cast<float *>(ws + p.part_off), reinterpret_cast<int *>(ws + p.counters_off),
+               reinterpret_cast<int *>(ws), W, S, H, Tn, p.qgs, p.bpu, p.total, p.per_warp, p.max_slots,
+               static_cast<float>(1.0 / 8.0 * 1.4426950408889634)};
+  const bool bf = dtype == WT_BF16;
+  const int g = p.grid, sh = p.shape;
+  switch (p.nt) {
+    case 1: return bf ? launch_stream_nt<__nv_bfloat16, 1>(km, vm, a, g, sh, stream) : launch_stream_nt<__half, 1>(km, vm, a, g, sh, stream);
+    case 2: return bf ? launch_stream_nt<__nv_bfloat16, 2>(km, vm, a, g, sh, stream) : launch_stream_nt<__half, 2>(km, vm, a, g, sh, stream);
+    case 3: return bf ? launch_stream_nt<__nv_bfloat16, 3>(km, vm, a, g, sh, stream) : launch_stream_nt<__half, 3>(km, vm, a, g, sh, stream);
+    default: return bf ? launch_stream_nt<__nv_bfloat16, 4>(km, vm, a, g, sh, stream) : launch_stream_nt<__half, 4>(km, vm, a, g, sh, stream);
+  }
+}
+
+}  // namespace wt

@@ -5,26 +5,52 @@
 // to [0, C], slot-table entries clamped to [0, N-1], the new token attended first and always, scores in log2 units
 // (scale d^-1/2 * log2 e), fp32 arithmetic on fp16/bf16 inputs, output in the input type.
 //
-// B200 design. The step is HBM-bound (about 1 FLOP per byte): each (row, head) streams `offset` gathered 128-byte
-// key rows and 128-byte value rows. One CTA of 4 warps per (row, head[, key split]):
-//   * the CTA's slot-table entries are staged in shared memory once, so every key/value load is issued without
-//     waiting on a dependent index load;
-//   * a key row is read by D/8 lanes with one 16-byte vector load each (a warp reads 4 whole 128-byte rows per
-//     instruction: every byte of every fetched sector is used); each lane keeps the matching 8 query elements, the
-//     dot product is finished with 3 butterfly shuffles;
-//   * each group of D/8 lanes runs its own online softmax over 4 keys per iteration, the groups and warps are
-//     merged at the end (shuffles, then shared memory);
-//   * kv_splits > 1 splits a row's cache range over CTAs; each writes its partial (acc, m, l) to the workspace and
-//     the last CTA of the (row, head) -- found with an atomic counter, no waiting -- combines them.
+// B200 design. The step is HBM-bound (about 1 FLOP per byte) and made of many short gathers: each (row, head)
+// streams `offset` 128-byte key rows and 128-byte value rows, each from the row its slot-table entry names.
+//   * one WARP per (row, head[, key split]); the 4 warps of a CTA take 4 heads of the same row and split, so they
+//     have the same length and no warp of a CTA waits for a longer one;
+//   * the warp stages its slot-table entries in shared memory once and at once sends every key/value row of its
+//     range towards L2 (bulk prefetches: all of the range's DRAM requests in flight together), then streams 16-key
+//     stages through a 3-deep cp.async ring (16-byte copies, bypassing L1): the loads in flight hold no registers,
+//     and the ring is laid out chunk-major ([chunk][lane]) so every read-back is bank-conflict free;
+//   * a key row is covered by D/8 lanes (one 16-byte piece each); the dot product is finished with 3 butterfly
+//     shuffles; each group of D/8 lanes runs its own online softmax (4 keys per stage), merged at the end;
+//   * kv_splits > 1 splits the cache capacity into equal static ranges; each split writes its partial (acc, m, l)
+//     to the workspace and the last warp of the (row, head) -- an atomic counter, no waiting -- combines them;
+//   * with programmatic dependent launch the offset, slot table and cache reads start before the preceding kernel
+//     has finished (only the new token's q/k/v wait for it).
 #include "common.cuh"
 
 namespace wt {
 namespace {
 
-constexpr int kSelfWarps = 4;
-constexpr int kSelfThreads = kSelfWarps * 32;
-constexpr int kKeysPerGroup = 4;  // keys per lane group per iteration
-constexpr int kMaxCapacity = 16384;
+constexpr int kWarpsPerCta = 4;  // = heads per CTA
+constexpr int kStages = 3;       // cp.async ring depth (stages of 16 keys)
+constexpr int kKeysPerGroup = 4;
+constexpr int kMaxSplitKeys = 256;  // keys per (row, head, split) staged in shared memory: splits >= ceil(C/256)
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Prefetch `bytes` (a multiple of 16) at a 16-byte aligned global address into L2.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 template <int LPK>
 __device__ __forceinline__ float group_sum(float x) {
@@ -38,48 +64,80 @@ __device__ __forceinline__ void merge_state(float &m, float &l, float (&acc)[8],
                                             const float (&acc2)[8]) {
   const float mn = fmaxf(m, m2);
   const float mu = (mn == kNegInf) ? 0.f : mn;
-  const float a1 = exp2f(m - mu), a2 = exp2f(m2 - mu);
+  const float a1 = ex2(m - mu), a2 = ex2(m2 - mu);
   l = l * a1 + l2 * a2;
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = acc[i] * a1 + acc2[i] * a2;
   m = mn;
 }
 
+// shared memory per warp: the ring ([stage][2 * 4 chunks][32 lanes] x 16 bytes), then the staged source rows
+constexpr int kRingBytes = kStages * 2 * kKeysPerGroup * 32 * 16;
+constexpr int kWarpSmem = kRingBytes + kMaxSplitKeys * 4;
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kSelfThreads)
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
     self_step_kernel(const T *__restrict__ qkv, T *kc, T *vc, const int64_t *__restrict__ offset,
                      const int32_t *__restrict__ src, T *__restrict__ y, float *__restrict__ part,
                      int *__restrict__ counters, int N, int H, int C, int write_cache, int splits, float scale) {
-  constexpr int LPK = D / 8;          // lanes per key row (16 bytes each)
-  constexpr int GPW = 32 / LPK;       // key groups per warp
+  constexpr int LPK = D / 8;     // lanes per key row (16 bytes each)
+  constexpr int GPW = 32 / LPK;  // key groups per warp
   constexpr int U = kKeysPerGroup;
-  constexpr int KPW = GPW * U;        // keys per warp per iteration
+  constexpr int KPS = GPW * U;   // keys per stage
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float *red = reinterpret_cast<float *>(smem_raw);                      // [warps][D + 2]
-  int *rows_s = reinterpret_cast<int *>(red + kSelfWarps * (D + 2));      // [range] source rows
-
-  const int rh = blockIdx.x, sp = blockIdx.y;
-  const int r = rh / H, h = rh - r * H;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int hgroups = (H + kWarpsPerCta - 1) / kWarpsPerCta;
+  const int r = blockIdx.x / hgroups, h = (blockIdx.x - r * hgroups) * kWarpsPerCta + warp;
+  const int sp = blockIdx.y;
+  if (h >= H) return;
   const int grp = lane / LPK, sub = lane % LPK;
   const size_t HD = static_cast<size_t>(H) * D;
+  unsigned char *ring = smem_raw + warp * kWarpSmem;
+  int *rows_s = reinterpret_cast<int *>(ring + kRingBytes);
 
-  pdl_wait();
-
-  const int64_t off64 = offset[r];
-  const int off = static_cast<int>(off64 < 0 ? 0 : (off64 > C ? C : off64));
-  const int per = (off + splits - 1) / splits;
-  const int lo = min(off, sp * per), hi = min(off, lo + per);
-
-  const int32_t *srow = src + static_cast<size_t>(r) * C;
-  for (int i = tid; i < hi - lo; i += kSelfThreads) {
-    const int v = srow[lo + i];
+  // Before waiting for the preceding kernel: the offset, this split's slot-table slice and the key/value rows it
+  // names (inputs the kernel launched just before this one does not write; the new token's q/k/v come after).
+  // Splits are static ranges of the capacity, so the slice is known without the offset.
+  const int cap = (C + splits - 1) / splits;
+  const int lo = sp * cap;
+  const int lim = min(C, lo + cap) - lo;
+  const int32_t *srow = src + static_cast<size_t>(r) * C + lo;
+  for (int i = lane; i < lim; i += 32) {
+    const int v = srow[i];
     rows_s[i] = v < 0 ? 0 : (v > N - 1 ? N - 1 : v);
   }
+  const int64_t off64 = offset[r];
+  const int off = static_cast<int>(off64 < 0 ? 0 : (off64 > C ? C : off64));
+  const int hi = max(lo, min(off, lo + cap));  // keys [lo, hi) of this split
+  __syncwarp();
 
+  const size_t row_stride = static_cast<size_t>(H) * C * D;
+  const T *kh = kc + static_cast<size_t>(h) * C * D + sub * 8;
+  const T *vh = vc + static_cast<size_t>(h) * C * D + sub * 8;
+  const int nst = (hi - lo + KPS - 1) / KPS;
+  // stage t: this lane's keys lo + t*KPS + grp*U + u; piece i (K: u, V: U + u) at ring[t % S][i][lane]
+  auto issue = [&](int t) {
+    unsigned char *slot = ring + (t % kStages) * (2 * U * 32 * 16);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = t * KPS + grp * U + u;  // relative to lo
+      if (j < hi - lo) {
+        const size_t o = static_cast<size_t>(rows_s[j]) * row_stride + static_cast<size_t>(lo + j) * D;
+        cp_async16(slot + (u * 32 + lane) * 16, kh + o);
+        cp_async16(slot + ((U + u) * 32 + lane) * 16, vh + o);
+      }
+    }
+  };
+#pragma unroll
+  for (int t = 0; t < kStages - 1; ++t) {
+    if (t < nst) issue(t);
+    cp_async_commit();
+  }
+
+  pdl_wait();
   const T *qrow = qkv + static_cast<size_t>(r) * 3 * HD + static_cast<size_t>(h) * D + sub * 8;
   const uint4 qraw = ldg16(qrow), kraw = ldg16(qrow + HD), vraw = ldg16(qrow + 2 * HD);
-  if (write_cache && sp == 0 && warp == 0 && grp == 0 && off < C) {
+  if (write_cache && sp == 0 && grp == 0 && off < C) {
     const size_t own = ((static_cast<size_t>(r) * H + h) * C + off) * D + sub * 8;
     *reinterpret_cast<uint4 *>(kc + own) = kraw;
     *reinterpret_cast<uint4 *>(vc + own) = vraw;
@@ -93,10 +151,9 @@ __global__ void __launch_bounds__(kSelfThreads)
 #pragma unroll
   for (int i = 0; i < 8; ++i) s_new = fmaf(q[i], kn[i], s_new);
   s_new = group_sum<LPK>(s_new);
-
-  // the new token first: every row attends to it (attn_plugin.py:331-334); one group of one CTA owns it
+  // the new token first: every row attends to it (attn_plugin.py:331-334); group 0 of split 0 owns it
   float m = kNegInf, l = 0.f, acc[8];
-  if (sp == 0 && warp == 0 && grp == 0) {
+  if (sp == 0 && grp == 0) {
     m = s_new;
     l = 1.f;
     unpack8<T>(vraw, acc);
@@ -104,32 +161,19 @@ __global__ void __launch_bounds__(kSelfThreads)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   }
-  __syncthreads();
 
-  const size_t row_stride = static_cast<size_t>(H) * C * D;
-  const T *kh = kc + static_cast<size_t>(h) * C * D + sub * 8;
-  const T *vh = vc + static_cast<size_t>(h) * C * D + sub * 8;
-  for (int k0 = lo + warp * KPW; k0 < hi; k0 += kSelfWarps * KPW) {
-    uint4 kr[U], vr[U];
+  for (int t = 0; t < nst; ++t) {
+    if (t + kStages - 1 < nst) issue(t + kStages - 1);
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();  // stage t has landed (this lane's copies)
+    const unsigned char *slot = ring + (t % kStages) * (2 * U * 32 * 16);
+    float s[U];
     bool ok[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = k0 + grp * U + u;
-      ok[u] = j < hi;
-      if (ok[u]) {
-        const size_t o = static_cast<size_t>(rows_s[j - lo]) * row_stride + static_cast<size_t>(j) * D;
-        kr[u] = ldg_stream(kh + o);
-        vr[u] = ldg_stream(vh + o);
-      } else {
-        kr[u] = make_uint4(0, 0, 0, 0);
-        vr[u] = kr[u];
-      }
-    }
-    float s[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
+      ok[u] = t * KPS + grp * U + u < hi - lo;
       float kf[8];
-      unpack8<T>(kr[u], kf);
+      unpack8<T>(*reinterpret_cast<const uint4 *>(slot + (u * 32 + lane) * 16), kf);
       float a = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) a = fmaf(q[i], kf[i], a);
@@ -145,21 +189,24 @@ __global__ void __launch_bounds__(kSelfThreads)
     }
     const float mn = fmaxf(m, mx);
     const float mu = (mn == kNegInf) ? 0.f : mn;
-    const float alpha = exp2f(m - mu);
+    const float alpha = ex2(m - mu);
     l *= alpha;
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] *= alpha;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float p = exp2f(s[u] - mu);
-      l += p;
-      float vf[8];
-      unpack8<T>(vr[u], vf);
+      if (ok[u]) {  // (a key past the range was never copied: its bytes are stale)
+        const float p = ex2(s[u] - mu);
+        l += p;
+        float vf[8];
+        unpack8<T>(*reinterpret_cast<const uint4 *>(slot + ((U + u) * 32 + lane) * 16), vf);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(p, vf[i], acc[i]);
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(p, vf[i], acc[i]);
+      }
     }
     m = mn;
   }
+  cp_async_wait<0>();
   pdl_launch_dependents();
 
   // merge the lane groups of the warp
@@ -171,52 +218,35 @@ __global__ void __launch_bounds__(kSelfThreads)
     for (int i = 0; i < 8; ++i) acc2[i] = __shfl_xor_sync(0xffffffffu, acc[i], o);
     merge_state(m, l, acc, m2, l2, acc2);
   }
-  // merge the warps
-  if (grp == 0) {
-    float *rw = red + warp * (D + 2);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) rw[sub * 8 + i] = acc[i];
-    if (sub == 0) {
-      rw[D] = m;
-      rw[D + 1] = l;
-    }
-  }
-  __syncthreads();
-  if (warp == 0 && grp == 0) {
-    for (int w2 = 1; w2 < kSelfWarps; ++w2) {
-      const float *rw = red + w2 * (D + 2);
-      float acc2[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc2[i] = rw[sub * 8 + i];
-      merge_state(m, l, acc, rw[D], rw[D + 1], acc2);
-    }
-    if (splits == 1) {
+  const int rh = r * H + h;
+  T *yo = y + static_cast<size_t>(r) * HD + static_cast<size_t>(h) * D + sub * 8;
+  if (splits == 1) {
+    if (grp == 0) {
       const float inv = 1.f / l;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] *= inv;
-      *reinterpret_cast<uint4 *>(y + static_cast<size_t>(r) * HD + static_cast<size_t>(h) * D + sub * 8) =
-          pack8<T>(acc);
-    } else {
-      float *pp = part + (static_cast<size_t>(rh) * splits + sp) * (D + 2);
+      *reinterpret_cast<uint4 *>(yo) = pack8<T>(acc);
+    }
+    return;
+  }
+  // the last split of this (row, head) to finish combines the partials
+  float *pp = part + (static_cast<size_t>(rh) * splits + sp) * (D + 2);
+  if (grp == 0) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pp[sub * 8 + i] = acc[i];
-      if (sub == 0) {
-        pp[D] = m;
-        pp[D + 1] = l;
-      }
+    for (int i = 0; i < 8; ++i) pp[sub * 8 + i] = acc[i];
+    if (sub == 0) {
+      pp[D] = m;
+      pp[D + 1] = l;
     }
   }
-  if (splits == 1) return;
-
-  // the last CTA of this (row, head) combines the splits' partials
-  __shared__ int is_last;
   __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = (atomicAdd(counters + rh, 1) == splits - 1);
-  __syncthreads();
-  if (!is_last) return;
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = (atomicAdd(counters + rh, 1) == splits - 1);
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
   __threadfence();
-  if (warp == 0 && grp == 0) {
+  if (grp == 0) {
     const float *pr = part + static_cast<size_t>(rh) * splits * (D + 2);
     float top = kNegInf;
     for (int s2 = 0; s2 < splits; ++s2) top = fmaxf(top, __ldcg(pr + s2 * (D + 2) + D));
@@ -224,7 +254,7 @@ __global__ void __launch_bounds__(kSelfThreads)
     for (int s2 = 0; s2 < splits; ++s2) {
       const float *p2 = pr + s2 * (D + 2);
       const float ms = __ldcg(p2 + D);
-      const float wgt = (ms == kNegInf) ? 0.f : exp2f(ms - top);
+      const float wgt = (ms == kNegInf) ? 0.f : ex2(ms - top);
       den = fmaf(wgt, __ldcg(p2 + D + 1), den);
 #pragma unroll
       for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(p2 + sub * 8 + i), num[i]);
@@ -232,10 +262,9 @@ __global__ void __launch_bounds__(kSelfThreads)
     const float inv = 1.f / den;
 #pragma unroll
     for (int i = 0; i < 8; ++i) num[i] *= inv;
-    *reinterpret_cast<uint4 *>(y + static_cast<size_t>(r) * HD + static_cast<size_t>(h) * D + sub * 8) =
-        pack8<T>(num);
+    *reinterpret_cast<uint4 *>(yo) = pack8<T>(num);
   }
-  if (tid == 0) counters[rh] = 0;  // left zeroed for the next launch
+  if (lane == 0) counters[rh] = 0;  // left zeroed for the next launch
 }
 
 size_t step_workspace(int rows, int heads, int head_dim, int splits) {
@@ -247,12 +276,10 @@ size_t step_workspace(int rows, int heads, int head_dim, int splits) {
 template <typename T, int D>
 int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y, int N,
                 int H, int C, int write_cache, int splits, void *ws, void *stream) {
-  const int range = (C + splits - 1) / splits;
-  const size_t smem = kSelfWarps * (D + 2) * sizeof(float) + static_cast<size_t>(range) * sizeof(int);
+  constexpr int smem = kWarpsPerCta * kWarpSmem;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(self_step_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kSelfWarps * (D + 2) * 4 + kMaxCapacity * 4);
+    cudaFuncSetAttribute(self_step_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr_set = true;
   }
   int *counters = nullptr;
@@ -263,8 +290,9 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
                                      (static_cast<size_t>(N) * H * sizeof(int) + 255) / 256 * 256);
   }
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(D)) * 1.4426950408889634);
-  return launch("self_attn_step", self_step_kernel<T, D>, dim3(N * H, splits), dim3(kSelfThreads), smem, stream,
-                static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
+  const int hgroups = (H + kWarpsPerCta - 1) / kWarpsPerCta;
+  return launch("self_attn_step", self_step_kernel<T, D>, dim3(N * hgroups, splits), dim3(kWarpsPerCta * 32), smem,
+                stream, static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
                 static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale);
 }
 
@@ -286,12 +314,13 @@ int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *off
 extern "C" {
 
 int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim) {
-  // one CTA per (row, head) already gives >= 4 CTAs of 4 warps per SM on 148 SMs: no split
-  const long long ctas = static_cast<long long>(rows) * heads;
-  const long long target = 148LL * 4;
-  if (ctas >= target || capacity <= 64) return 1;
-  long long s = (target + ctas - 1) / ctas;
-  const long long cap = capacity / 32;  // at least ~32 keys per split
+  // one warp per (row, head, split), at most 256 slots each; split further only when the (row, head) pairs alone
+  // would leave the SMs short of warps (< 4 per SM): measured, splitting costs more than it hides otherwise
+  const long long items = static_cast<long long>(rows) * heads;
+  long long s = (capacity + 255) / 256;
+  const long long want = (148LL * 4 + items - 1) / items;
+  if (want > s) s = want;
+  const long long cap = (capacity + 31) / 32;  // at least ~32 keys per split
   if (s > cap) s = cap;
   if (s < 1) s = 1;
   if (s > 64) s = 64;
@@ -317,12 +346,15 @@ int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, 
   WT_ALIGNED(offset);
   WT_ALIGNED(src);
   WT_ALIGNED(y);
-  WT_REQUIRE(capacity <= kMaxCapacity, WT_ERR_UNSUPPORTED, "self_attn_step: capacity %d > %d", capacity,
-             kMaxCapacity);
-  WT_REQUIRE(static_cast<long long>(rows) * heads < (1LL << 31), WT_ERR_ARG, "self_attn_step: rows*heads too large");
+  WT_REQUIRE(static_cast<long long>(rows) * ((heads + kWarpsPerCta - 1) / kWarpsPerCta) < (1LL << 31), WT_ERR_ARG,
+             "self_attn_step: rows*heads too large");
   int splits = kv_splits > 0 ? kv_splits : wt_self_attn_step_splits(rows, heads, capacity, head_dim);
   if (splits > capacity) splits = capacity;
   WT_REQUIRE(splits <= 65535, WT_ERR_ARG, "self_attn_step: kv_splits %d too large", splits);
+  WT_REQUIRE((capacity + splits - 1) / splits <= kMaxSplitKeys, WT_ERR_ARG,
+             "self_attn_step: %d cache slots per split (capacity %d / %d splits) > %d: kv_splits must be at least "
+             "ceil(capacity / %d)",
+             (capacity + splits - 1) / splits, capacity, splits, kMaxSplitKeys, kMaxSplitKeys);
   if (splits > 1) {
     const size_t need = step_workspace(rows, heads, head_dim, splits);
     WT_REQUIRE(workspace && workspace_bytes >= need, WT_ERR_WORKSPACE,

@@ -78,6 +78,16 @@ def _workspace(dev: torch.device, kind: str, shape: tuple, nbytes: int) -> torch
     return ws
 
 
+def workspace_errors() -> int:
+    """The device error words of this process's cross-attention workspaces, OR-ed (0: no kernel gave up a wait).
+    Reads device memory: synchronises."""
+    err = 0
+    for (dev, kind, shape), ws in _workspaces.items():
+        if kind == "cross":
+            err |= int(ws[:4].view(torch.int32).item())
+    return err
+
+
 def _qk_scale(d: int) -> float:
     return d**-0.5 * math.log2(math.e)
 
@@ -97,7 +107,7 @@ def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     caches at ``offset`` (in place). Reference: attn_plugin.py:488-501 (kernel :309-350).
 
     ``config`` is accepted for call-compatibility and ignored; ``kv_splits`` (None: chosen from the shape) splits
-    every row's cache over that many CTAs."""
+    every row's cache into that many parts (at least ceil(C / 256))."""
     what = "self_attn_step"
     if qkv.dim() != 3:
         raise ValueError(f"{what}: qkv must be [N, S, 3*H*D]")
@@ -122,6 +132,7 @@ def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         raise ValueError(f"{what}: out must be [N, 1, H*D] of qkv's dtype")
     lib = _lib.load()
     splits = int(kv_splits) if kv_splits else int(lib.wt_self_attn_step_splits(n, h, c, d))
+    splits = max(splits, -(-c // 256))  # (at most 256 cache slots per split)
     ws_ptr, ws_bytes = None, 0
     if splits > 1:
         ws_bytes = int(lib.wt_self_attn_step_workspace(n, h, d, splits))
