@@ -122,10 +122,13 @@ class Schedule:
 
 
 def initial_src(W: int, K: int, C: int, seed: int) -> np.ndarray:
-    """Each slot of a row from a random beam of its window (config 1's distribution)."""
+    """The slot tables at the start: each slot column of a window a random permutation of its beams' rows -- what
+    random parent permutations produce -- so every row reads distinct cache rows (no two rows of a window share a
+    (row, slot), so the bytes counted are the bytes the kernels must fetch)."""
     rng = np.random.default_rng(seed + 7)
-    base = (np.arange(W * K) // K * K)[:, None]
-    return (base + rng.integers(0, K, (W * K, C))).astype(np.int32)
+    perm = np.argsort(rng.random((W, C, K)), axis=2)  # [W, C, K]: a permutation of the K beams per (window, slot)
+    rows = (np.arange(W)[:, None, None] * K + perm).transpose(0, 2, 1).reshape(W * K, C)
+    return rows.astype(np.int32)
 
 
 def measured_hbm_peak() -> tuple[float, str]:

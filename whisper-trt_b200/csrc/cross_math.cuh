@@ -76,12 +76,12 @@ __device__ __forceinline__ float ex2(float x) {
 //   va[i]  : A fragment (16 head dims x 16 keys) of head-dim tile i of O^T = V^T P^T
 //   qf[nt] : B fragments of the queries, k-step s in qf[nt][2s], qf[nt][2s+1]
 //   ok0/ok8: keys g and g+8 of the block exist (masked to -inf otherwise)
-// P is rounded to the input type for the P.V product (bf16: split into hi + lo parts, two products) and the row
-// sums use the rounded values, so numerator and denominator see the same weights.
+// P enters the P.V product as hi + lo parts in the input type (two products: fp16 keeps ~22 bits of each weight,
+// bf16 ~16) and the row sums use the same split values, so numerator and denominator see the same weights.
 template <typename T, int NT>
 __device__ __forceinline__ void attend_block(State<NT> &st, const uint32_t (&ka)[4][4], const uint32_t (&va)[4][4],
                                              const uint32_t (&qf)[NT][8], bool ok0, bool ok8, float scale) {
-  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool kSplitP = true;  // P = hi + lo in the input type: ~22 bits of each weight reach the P.V product
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -138,7 +138,7 @@ template <typename T, int NT>
 __device__ __forceinline__ void attend_block2(State<NT> &st, const uint32_t (&ka0)[4][4], const uint32_t (&va0)[4][4],
                                               const uint32_t (&ka1)[4][4], const uint32_t (&va1)[4][4],
                                               const uint32_t (&qf)[NT][8], const bool (&ok)[2][2], float scale) {
-  constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool kSplitP = true;  // P = hi + lo in the input type: ~22 bits of each weight reach the P.V product
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};

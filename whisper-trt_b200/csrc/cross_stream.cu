@@ -71,9 +71,13 @@ __device__ __forceinline__ void reset_state(State<NT> &st) {
   }
 }
 
-// The warp's partial for unit u (its `nblk` blocks of it) -> workspace; the warp that completes u combines.
-template <typename T, int NT>
-__device__ void flush_unit(State<NT> &st, const StreamArgs &a, long long u, int nblk, long long gw, int lane) {
+// The warp's partial for unit u (its `nblk` blocks of it) -> workspace, then its block count added to the unit's
+// counter with release semantics (one lane, after a warp barrier: no fence stalls the streaming warp). Returns, in
+// lane 0, whether this warp completed the unit -- the caller looks at it only when its range is done, so the
+// atomic's round trip never stalls the stream.
+template <int NT>
+__device__ __forceinline__ int write_partial(State<NT> &st, const StreamArgs &a, long long u, int nblk, long long gw,
+                                             int lane) {
   const int g = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -99,13 +103,21 @@ __device__ void flush_unit(State<NT> &st, const StreamArgs &a, long long u, int 
         rq[kD + 1] = st.l[nt][j];
       }
     }
-  __threadfence();
   __syncwarp();
-  int last = 0;
-  if (lane == 0) last = (atomicAdd(a.counters + u, nblk) + nblk == a.bpu);
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  __threadfence();
+  int old = 0;
+  if (lane == 0)
+    asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "l"(a.counters + u), "r"(nblk)
+                 : "memory");
+  return old + nblk == a.bpu;
+}
+
+// The warp that completed unit u: every partial of u -> the output (then the counter back to zero).
+template <typename T, int NT>
+__device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  const long long fw = first_warp(u, a.bpu, a.per_warp);
   const int nslots = static_cast<int>(last_warp(u, a.bpu, a.per_warp) - fw + 1);
   const int wh = static_cast<int>(u / a.QG), qg = static_cast<int>(u % a.QG);
   const int w = wh / a.H, h = wh - w * a.H;
@@ -195,13 +207,31 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1)
   long long cur = -1;
   int nblk = 0;
   uint32_t late = 0;  // stages whose wait timed out (their copies may still be in flight)
+  // units this warp flushed and must combine if it turned out to complete them (lane 0 knows), at most two pending
+  long long pend_u0 = -1, pend_u1 = -1;
+  int pend_l0 = 0, pend_l1 = 0;
+  auto flush = [&](long long u, int nb) {
+    const int last = write_partial<NT>(st, a, u, nb, gw, lane);
+    if (pend_u0 < 0) {
+      pend_u0 = u;
+      pend_l0 = last;
+    } else {
+      if (pend_u1 >= 0) {  // (a third unit: settle the oldest now)
+        if (__shfl_sync(0xffffffffu, pend_l0, 0)) combine_unit<T, NT>(a, pend_u0, lane);
+        pend_u0 = pend_u1;
+        pend_l0 = pend_l1;
+      }
+      pend_u1 = u;
+      pend_l1 = last;
+    }
+  };
   int c_wh = static_cast<int>(u0 / a.QG), c_qg = static_cast<int>(u0 % a.QG);
   int c_b = static_cast<int>(beg - u0 * a.bpu);
   long long c_u = u0;
   for (int j = 0; j < n;) {
     if (c_u != cur) {
       if (cur >= 0) {
-        flush_unit<T, NT>(st, a, cur, nblk, gw, lane);
+        flush(cur, nblk);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -268,7 +298,9 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1)
       }
     }
   }
-  if (cur >= 0) flush_unit<T, NT>(st, a, cur, nblk, gw, lane);
+  if (cur >= 0) flush(cur, nblk);
+  if (pend_u0 >= 0 && __shfl_sync(0xffffffffu, pend_l0, 0)) combine_unit<T, NT>(a, pend_u0, lane);
+  if (pend_u1 >= 0 && __shfl_sync(0xffffffffu, pend_l1, 0)) combine_unit<T, NT>(a, pend_u1, lane);
   // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
   for (int j = n - min(n, kStreamStages); j < n; ++j) {
     const int s = j % kStreamStages;

@@ -25,7 +25,8 @@ namespace wt {
 namespace {
 
 constexpr int kWarpsPerCta = 4;  // = heads per CTA
-constexpr int kStages = 3;       // cp.async ring depth (stages of 16 keys)
+constexpr int kStages = 2;       // cp.async ring depth (stages of 16 keys): the L2 prefetch covers the latency,
+                                 // a shallow ring keeps 6 CTAs (24 warps) per SM resident
 constexpr int kKeysPerGroup = 4;
 constexpr int kMaxSplitKeys = 256;  // keys per (row, head, split) staged in shared memory: splits >= ceil(C/256)
 
@@ -34,6 +35,38 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// acc += a * b for two packed 16-bit pairs, each product and sum in fp32 (the fp16 values convert exactly, so this
+// equals unpacking then fma.f32): sm_100 mixed-precision FMA, no unpack instructions.
+template <typename T> struct MixFma;
+template <> struct MixFma<__half> {
+  static __device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float acc) {
+    asm("{\n"
+        ".reg .b16 alo, ahi, blo, bhi;\n"
+        "mov.b32 {alo, ahi}, %1;\n"
+        "mov.b32 {blo, bhi}, %2;\n"
+        "fma.rn.f32.f16 %0, alo, blo, %0;\n"
+        "fma.rn.f32.f16 %0, ahi, bhi, %0;\n"
+        "}\n"
+        : "+f"(acc)
+        : "r"(a), "r"(b));
+    return acc;
+  }
+};
+template <> struct MixFma<__nv_bfloat16> {
+  static __device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float acc) {
+    asm("{\n"
+        ".reg .b16 alo, ahi, blo, bhi;\n"
+        "mov.b32 {alo, ahi}, %1;\n"
+        "mov.b32 {blo, bhi}, %2;\n"
+        "fma.rn.f32.bf16 %0, alo, blo, %0;\n"
+        "fma.rn.f32.bf16 %0, ahi, bhi, %0;\n"
+        "}\n"
+        : "+f"(acc)
+        : "r"(a), "r"(b));
+    return acc;
+  }
+};
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
@@ -142,15 +175,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     *reinterpret_cast<uint4 *>(kc + own) = kraw;
     *reinterpret_cast<uint4 *>(vc + own) = vraw;
   }
-  float q[8], kn[8];
-  unpack8<T>(qraw, q);
-  unpack8<T>(kraw, kn);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] *= scale;
+  const uint32_t qw[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
   float s_new = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) s_new = fmaf(q[i], kn[i], s_new);
-  s_new = group_sum<LPK>(s_new);
+  s_new = MixFma<T>::dot2(qw[0], kraw.x, s_new);
+  s_new = MixFma<T>::dot2(qw[1], kraw.y, s_new);
+  s_new = MixFma<T>::dot2(qw[2], kraw.z, s_new);
+  s_new = MixFma<T>::dot2(qw[3], kraw.w, s_new);
+  s_new = group_sum<LPK>(s_new) * scale;  // (the scale after the dot product, as attn_plugin.py:332)
   // the new token first: every row attends to it (attn_plugin.py:331-334); group 0 of split 0 owns it
   float m = kNegInf, l = 0.f, acc[8];
   if (sp == 0 && grp == 0) {
@@ -172,15 +203,16 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       ok[u] = t * KPS + grp * U + u < hi - lo;
-      float kf[8];
-      unpack8<T>(*reinterpret_cast<const uint4 *>(slot + (u * 32 + lane) * 16), kf);
+      const uint4 kw = *reinterpret_cast<const uint4 *>(slot + (u * 32 + lane) * 16);
       float a = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) a = fmaf(q[i], kf[i], a);
+      a = MixFma<T>::dot2(qw[0], kw.x, a);
+      a = MixFma<T>::dot2(qw[1], kw.y, a);
+      a = MixFma<T>::dot2(qw[2], kw.z, a);
+      a = MixFma<T>::dot2(qw[3], kw.w, a);
       s[u] = a;
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) s[u] = group_sum<LPK>(s[u]);
+    for (int u = 0; u < U; ++u) s[u] = group_sum<LPK>(s[u]) * scale;
     float mx = kNegInf;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -267,6 +299,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   if (lane == 0) counters[rh] = 0;  // left zeroed for the next launch
 }
 
+
 size_t step_workspace(int rows, int heads, int head_dim, int splits) {
   if (splits <= 1) return 0;
   const size_t counters = (static_cast<size_t>(rows) * heads * sizeof(int) + 255) / 256 * 256;
@@ -277,9 +310,10 @@ template <typename T, int D>
 int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y, int N,
                 int H, int C, int write_cache, int splits, void *ws, void *stream) {
   constexpr int smem = kWarpsPerCta * kWarpSmem;
+  auto kernel = self_step_kernel<T, D>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(self_step_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr_set = true;
   }
   int *counters = nullptr;
@@ -291,8 +325,7 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
   }
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(D)) * 1.4426950408889634);
   const int hgroups = (H + kWarpsPerCta - 1) / kWarpsPerCta;
-  return launch("self_attn_step", self_step_kernel<T, D>, dim3(N * hgroups, splits), dim3(kWarpsPerCta * 32), smem,
-                stream, static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
+  return launch("self_attn_step", kernel, dim3(N * hgroups, splits), dim3(kWarpsPerCta * 32), smem, stream, static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
                 static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale);
 }
 
