@@ -56,7 +56,10 @@ int launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 }
 
 // ---- device side -----------------------------------------------------------------------------------------
-// Programmatic dependent launch controls (no-ops when the kernel was launched without the attribute).
+// Programmatic dependent launch controls (no-ops when the kernel was launched without the attribute). The kernels
+// trigger their dependents right after their own wait: a dependent then starts while this kernel works, but no
+// earlier than this kernel's predecessor has completed, so "not written by the kernel launched just before" is all
+// a kernel's pre-wait reads need.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -33,8 +33,9 @@ constexpr int kErrTimeout = 1;
 struct Shape {
   int warps, stages;
   bool pair;  // two 16-key blocks per step of the online softmax
+  int ctas;   // CTAs per SM
 };
-constexpr Shape kShapes[] = {{12, 4, false}, {12, 4, true}, {8, 6, true}, {10, 5, true}, {16, 3, false}};
+constexpr Shape kShapes[] = {{12, 4, false, 1}, {12, 4, true, 1}, {6, 4, true, 2}, {8, 4, true, 1}, {4, 4, true, 3}};
 
 constexpr int smem_bytes(int warps, int stages) { return warps * stages * kStageBytes + warps * stages * 8 + 1024; }
 
@@ -149,7 +150,7 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
 }
 
 template <typename T, int NT, int kStreamWarps, int kStreamStages, bool kPair>
-__global__ void __launch_bounds__(kStreamWarps * 32, 1)
+__global__ void __launch_bounds__(kStreamWarps * 32)
     cross_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                         const StreamArgs a) {
   constexpr int kWarpRing = kStreamStages * kStageBytes;
@@ -199,6 +200,9 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1)
   // (everything above reads only the cross keys/values, which the kernel launched just before this one does not
   // write; the queries, the workspace and the output wait for it)
   pdl_wait();
+  // the next kernel may launch now: it reads nothing this kernel writes before its own wait, which waits for
+  // this kernel to complete
+  pdl_launch_dependents();
 
   const T *q = static_cast<const T *>(a.q);
   const size_t HD = static_cast<size_t>(a.H) * kD;
@@ -306,7 +310,6 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1)
     const int s = j % kStreamStages;
     if (late & (1u << s)) mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kStreamStages) & 1), nullptr, 0);
   }
-  pdl_launch_dependents();
 }
 
 int g_sm_count[64] = {};
@@ -327,8 +330,8 @@ int shape_index() {
   static int idx = -1;
   if (idx < 0) {
     const char *e = getenv("WT_CROSS_SHAPE");
-    int v = e ? atoi(e) : 1;
-    idx = (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : 1;
+    int v = e ? atoi(e) : 2;
+    idx = (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : 2;
   }
   return idx;
 }
@@ -346,8 +349,8 @@ StreamPlan plan_stream(int W, int S, int H, int Tn) {
   p.bpu = (Tn + 15) / 16;
   p.units = static_cast<long long>(W) * H * p.qgs;
   p.total = p.units * p.bpu;
-  p.grid = sm_count();
   p.shape = p.nt >= 2 ? 0 : shape_index();  // (more query tiles: one block per step keeps them in registers)
+  p.grid = sm_count() * kShapes[p.shape].ctas;
   const long long warps = static_cast<long long>(p.grid) * kShapes[p.shape].warps;
   p.per_warp = (p.total + warps - 1) / warps;
   p.max_slots = static_cast<int>((p.bpu + p.per_warp - 1) / p.per_warp + 1);

@@ -168,6 +168,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   }
 
   pdl_wait();
+  // the next kernel may launch now: it reads nothing this kernel writes before its own wait, which waits for
+  // this kernel to complete
+  pdl_launch_dependents();
   const T *qrow = qkv + static_cast<size_t>(r) * 3 * HD + static_cast<size_t>(h) * D + sub * 8;
   const uint4 qraw = ldg16(qrow), kraw = ldg16(qrow + HD), vraw = ldg16(qrow + 2 * HD);
   if (write_cache && sp == 0 && grp == 0 && off < C) {
@@ -239,7 +242,6 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     m = mn;
   }
   cp_async_wait<0>();
-  pdl_launch_dependents();
 
   // merge the lane groups of the warp
 #pragma unroll

@@ -1,5 +1,5 @@
 // Tensor Memory Accelerator (TMA) and mbarrier helpers for sm_100a: tensor maps encoded on the host through the
-// driver entry point, 2D tiled bulk loads into shared memory completing on an mbarrier (no multicast anywhere), and
+// driver entry point, 2D tiled bulk loads into shared memory completing on an mbarrier, and
 // bounded mbarrier waits that record a timeout instead of spinning forever.
 #pragma once
 
