@@ -83,6 +83,17 @@ int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, 
                       int write_cache, int kv_splits, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------------------------------------------
+ * Self-attention of S = new_tokens new tokens per row (a prompt) over the row's cache slots < offset[r] (each read
+ * from the row src[r, j] names) and, causally, the new tokens up to itself.
+ * Replaces attn_plugin.py:462-479 self_attn_triton (kernel :275-307; op body :102-121).
+ *   qkv [N, S, 3*H*D], caches [N, H, C, D] (read only: the caller stores the new keys/values), y [N, S, H*D].
+ *   head_dim 64. No workspace; offset clamped to [0, C], slot-table rows to [0, N-1].
+ * ------------------------------------------------------------------------------------------------------- */
+int wt_self_attn(int dtype, const void *qkv, const void *k_cache, const void *v_cache, const int64_t *offset,
+                 const int32_t *src, void *y, int rows, int new_tokens, int heads, int capacity, int head_dim,
+                 void *stream);
+
+/* ---------------------------------------------------------------------------------------------------------
  * Cross-attention, split over the T keys ("flash-decoding").
  * wt_cross_attn_split replaces attn_plugin.py:521-534 cross_attn_split_triton (kernel :378-409): slice i of
  *   chunk = ceil(T / splits) keys -> part[w, h, i, s, :] = (sum_j p_j v_j, m, sum_j p_j) with m the slice's

@@ -64,6 +64,14 @@ def test_bad_arguments_return_status_without_a_gpu():
     assert st == _lib.WT_ERR_WORKSPACE
     st = lib.wt_cross_attn(0, p, p, p, p, 2, 5, 20, 1500, 64, None, 0, None)
     assert st == _lib.WT_ERR_WORKSPACE
+    st = lib.wt_self_attn(0, p, p, p, p, p, p, 4, 0, 20, 96, 64, None)
+    assert st == _lib.WT_ERR_ARG and b"sizes" in lib.wt_last_error()
+    st = lib.wt_self_attn(0, p, p, p, p, p, p + 8, 4, 3, 20, 96, 64, None)
+    assert st == _lib.WT_ERR_ALIGN and b"y" in lib.wt_last_error()
+    st = lib.wt_self_attn(0, p, p, p, p, p, p, 4, 3, 20, 96, 32, None)
+    assert st == _lib.WT_ERR_UNSUPPORTED
+    st = lib.wt_self_attn(5, p, p, p, p, p, p, 4, 3, 20, 96, 64, None)
+    assert st == _lib.WT_ERR_DTYPE
     st = lib.wt_cross_attn_split(0, p, p, p, p, 2, 5, 20, 1500, 32, 8, None)
     assert st == _lib.WT_ERR_UNSUPPORTED
     st = lib.wt_beam_reorder(p, None, None, None, p, p, None, None, 2, 64, 8, 0, 1, None)
@@ -141,4 +149,5 @@ def test_install_routes_a_module():
     mod = types.SimpleNamespace()
     attn_plugin.install(mod)
     assert mod.self_attn_step_triton is attn_plugin.self_attn_step_triton
+    assert mod.self_attn_triton is attn_plugin.self_attn_triton
     assert mod.cross_attn_combine_triton is attn_plugin.cross_attn_combine_triton

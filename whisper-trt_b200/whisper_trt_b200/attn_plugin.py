@@ -145,6 +145,42 @@ def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     return y
 
 
+def self_attn_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: torch.Tensor,
+                     src: torch.Tensor, config=None, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Self-attention of S new tokens per row (qkv [N, S, 3*H*D], a prompt) over the row's cache slots < offset,
+    read through ``src``, and causally over the new tokens -> [N, S, H*D] in qkv's dtype. The caches are only read
+    (the caller stores the new keys/values). Reference: attn_plugin.py:462-479 (kernel :275-307, op :102-121).
+
+    ``config`` is accepted for call-compatibility and ignored (one launch shape: 64 queries per CTA)."""
+    what = "self_attn"
+    if qkv.dim() != 3:
+        raise ValueError(f"{what}: qkv must be [N, S, 3*H*D]")
+    n, s, _ = qkv.shape
+    if k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
+        raise ValueError(f"{what}: k_cache/v_cache must be [N, H, C, D] of the same shape")
+    h, c, d = k_cache.shape[1:]
+    if k_cache.shape[0] != n or qkv.shape[2] != 3 * h * d:
+        raise ValueError(f"{what}: qkv {tuple(qkv.shape)} does not match the cache {tuple(k_cache.shape)}")
+    if offset.shape != (n,) or offset.dtype != torch.int64:
+        raise ValueError(f"{what}: offset must be [N] int64")
+    if src.shape != (n, c) or src.dtype != torch.int32:
+        raise ValueError(f"{what}: src must be [N, C] int32")
+    code = _dtype_code(qkv, what)
+    if k_cache.dtype != qkv.dtype or v_cache.dtype != qkv.dtype:
+        raise TypeError(f"{what}: the caches must have qkv's dtype")
+    dev = _cuda(what, qkv, k_cache, v_cache, offset, src)
+    y = qkv.new_empty(n, s, h * d) if out is None else out
+    if y.shape != (n, s, h * d) or y.dtype != qkv.dtype:
+        raise ValueError(f"{what}: out must be [N, S, H*D] of qkv's dtype")
+    if s == 0:
+        return y
+    with torch.cuda.device(dev):
+        st = _lib.load().wt_self_attn(code, qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), offset.data_ptr(),
+                                      src.data_ptr(), y.data_ptr(), n, s, h, c, d, _stream(dev))
+    _lib.check(st, what)
+    return y
+
+
 def cache_append(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: torch.Tensor) -> None:
     """Row r's new key/value (from qkv [N, 1, 3*H*D]) into its own cache slot offset[r] (if < C), in place: the
     scatter of the reference's search.py:249-250 for one layer (the append of attn_plugin.py:327-330 alone)."""
@@ -252,6 +288,21 @@ def cross_attn_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, config=
 
 
 # --- torch custom ops (graph-capturable, with fake kernels for tracing) ------------------------------------
+@torch.library.custom_op(f"{NAMESPACE}::self_attn", mutates_args=())
+def self_attn(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: torch.Tensor,
+              src: torch.Tensor) -> torch.Tensor:
+    """Self-attention of S new tokens per row through the slot table (reference op ``whisper_trt::self_attn``,
+    attn_plugin.py:102-121): the one-token step kernel for S = 1, the prompt kernel otherwise."""
+    if qkv.shape[1] == 1:
+        return self_attn_step_triton(qkv, k_cache, v_cache, offset, src)
+    return self_attn_triton(qkv, k_cache, v_cache, offset, src)
+
+
+@self_attn.register_fake
+def _(qkv, k_cache, v_cache, offset, src):
+    return qkv.new_empty(qkv.shape[0], qkv.shape[1], k_cache.shape[1] * k_cache.shape[3])
+
+
 @torch.library.custom_op(f"{NAMESPACE}::self_attn_step", mutates_args=())
 def self_attn_step(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: torch.Tensor,
                    src: torch.Tensor) -> torch.Tensor:
@@ -309,6 +360,6 @@ def _(part, q):
 def install(module) -> None:
     """Route a reference ``whisper_trt.attn_plugin`` module's launchers to these kernels (in place), so its callers
     -- ``TritonDecoderBackend.step_fn`` (runtime.py:134-151) among them -- run on them unchanged."""
-    for name in ("self_attn_step_triton", "cross_attn_split_triton", "cross_attn_combine_triton",
-                 "cross_attn_triton", "self_attn_step_config"):
+    for name in ("self_attn_triton", "self_attn_step_triton", "cross_attn_split_triton",
+                 "cross_attn_combine_triton", "cross_attn_triton", "self_attn_step_config"):
         setattr(module, name, globals()[name])
