@@ -28,6 +28,7 @@ namespace {
 constexpr int kTileBytes = 16 * 128;         // 16 keys x 64 elements x 2 bytes
 constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
 constexpr int kErrTimeout = 1;
+constexpr int kPart = kD + 4;  // floats per query of a partial: acc[64], m, l, 2 pad (16-byte aligned records)
 
 // Launch shapes: warps per CTA (one CTA per SM) x ring stages per warp. Shared memory: warps * stages * 4 KB.
 struct Shape {
@@ -88,12 +89,12 @@ __device__ __forceinline__ int write_partial(State<NT> &st, const StreamArgs &a,
       for (int o = 4; o < 32; o <<= 1) st.l[nt][j] += __shfl_xor_sync(0xffffffffu, st.l[nt][j], o);
   const long long fw = first_warp(u, a.bpu, a.per_warp);
   const int slot = static_cast<int>(gw - fw);
-  float *dst = a.part + (static_cast<size_t>(u) * a.max_slots + slot) * (NT * 8) * (kD + 2);
+  float *dst = a.part + (static_cast<size_t>(u) * a.max_slots + slot) * (NT * 8) * kPart;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      float *rq = dst + (nt * 8 + 2 * c + j) * (kD + 2);
+      float *rq = dst + (nt * 8 + 2 * c + j) * kPart;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         rq[16 * i + g] = st.o[nt][i][j];
@@ -114,7 +115,11 @@ __device__ __forceinline__ int write_partial(State<NT> &st, const StreamArgs &a,
   return old + nblk == a.bpu;
 }
 
-// The warp that completed unit u: every partial of u -> the output (then the counter back to zero).
+// The warp that completed unit u: every partial of u -> the output (then the counter back to zero). Each lane owns
+// (query, 8-dim chunk) items; for a pass of up to kCombineSlots partials it issues every load first (one L2 round
+// trip), then folds them into a running (top, den, num) -- the reference's combine (attn_plugin.py:182-194), merged
+// pass by pass.
+constexpr int kCombineSlots = 4;
 template <typename T, int NT>
 __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
@@ -124,27 +129,80 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
   const int w = wh / a.H, h = wh - w * a.H;
   const int q0 = qg * NT * 8;
   const int nq = min(NT * 8, a.S - q0);
-  const float *base = a.part + static_cast<size_t>(u) * a.max_slots * (NT * 8) * (kD + 2);
+  const float *base = a.part + static_cast<size_t>(u) * a.max_slots * (NT * 8) * kPart;
   const size_t HD = static_cast<size_t>(a.H) * kD;
   T *y = static_cast<T *>(a.y);
-  for (int idx = lane; idx < nq * (kD / 8); idx += 32) {
-    const int qq = idx / (kD / 8), d8 = idx - qq * (kD / 8);
-    float top = kNegInf;
-    for (int s2 = 0; s2 < nslots; ++s2) top = fmaxf(top, __ldcg(base + (s2 * NT * 8 + qq) * (kD + 2) + kD));
-    float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
-    for (int s2 = 0; s2 < nslots; ++s2) {
-      const float *ps = base + (s2 * NT * 8 + qq) * (kD + 2);
-      const float ms = __ldcg(ps + kD);
-      const float wgt = (ms == kNegInf) ? 0.f : exp2f(ms - top);
-      den = fmaf(wgt, __ldcg(ps + kD + 1), den);
+  constexpr int kItems = NT * 8 * (kD / 8) / 32;  // items per lane (NT * 2)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(ps + 8 * d8 + i), num[i]);
+  for (int it0 = 0; it0 < kItems; it0 += 2) {
+    float top[2], den[2], num[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      top[k] = kNegInf;
+      den[k] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) num[k][i] = 0.f;
     }
-    const float inv = 1.f / den;
+    for (int s0 = 0; s0 < nslots; s0 += kCombineSlots) {
+      float ml[2][kCombineSlots][2];
+      float4 av[2][kCombineSlots][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) num[i] *= inv;
-    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * a.S + q0 + qq) * HD + static_cast<size_t>(h) * kD +
-                               8 * d8) = pack8<T>(num);
+      for (int k = 0; k < 2; ++k) {
+        const int idx = lane + 32 * (it0 + k), qq = idx >> 3, d8 = idx & 7;
+#pragma unroll
+        for (int s2 = 0; s2 < kCombineSlots; ++s2) {
+          if (qq < nq && s0 + s2 < nslots) {
+            const float *ps = base + ((s0 + s2) * NT * 8 + qq) * kPart;
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(ps + kD));
+            ml[k][s2][0] = v.x;
+            ml[k][s2][1] = v.y;
+            av[k][s2][0] = __ldcg(reinterpret_cast<const float4 *>(ps + 8 * d8));
+            av[k][s2][1] = __ldcg(reinterpret_cast<const float4 *>(ps + 8 * d8 + 4));
+          } else {
+            ml[k][s2][0] = kNegInf;
+            ml[k][s2][1] = 0.f;
+            av[k][s2][0] = av[k][s2][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float nt_top = top[k];
+#pragma unroll
+        for (int s2 = 0; s2 < kCombineSlots; ++s2) nt_top = fmaxf(nt_top, ml[k][s2][0]);
+        if (nt_top == kNegInf) continue;  // (no keys yet: nothing to fold)
+        const float f = top[k] == kNegInf ? 0.f : ex2(top[k] - nt_top);
+        den[k] *= f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) num[k][i] *= f;
+        top[k] = nt_top;
+#pragma unroll
+        for (int s2 = 0; s2 < kCombineSlots; ++s2) {
+          const float wgt = ml[k][s2][0] == kNegInf ? 0.f : ex2(ml[k][s2][0] - nt_top);
+          den[k] = fmaf(wgt, ml[k][s2][1], den[k]);
+          const float4 x = av[k][s2][0], z = av[k][s2][1];
+          num[k][0] = fmaf(wgt, x.x, num[k][0]);
+          num[k][1] = fmaf(wgt, x.y, num[k][1]);
+          num[k][2] = fmaf(wgt, x.z, num[k][2]);
+          num[k][3] = fmaf(wgt, x.w, num[k][3]);
+          num[k][4] = fmaf(wgt, z.x, num[k][4]);
+          num[k][5] = fmaf(wgt, z.y, num[k][5]);
+          num[k][6] = fmaf(wgt, z.z, num[k][6]);
+          num[k][7] = fmaf(wgt, z.w, num[k][7]);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int idx = lane + 32 * (it0 + k), qq = idx >> 3, d8 = idx & 7;
+      if (qq < nq) {
+        const float inv = 1.f / den[k];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) num[k][i] *= inv;
+        *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * a.S + q0 + qq) * HD + static_cast<size_t>(h) * kD +
+                                   8 * d8) = pack8<T>(num[k]);
+      }
+    }
   }
   if (lane == 0) a.counters[u] = 0;  // left zeroed for the next launch
 }
@@ -356,7 +414,7 @@ StreamPlan plan_stream(int W, int S, int H, int Tn) {
   p.max_slots = static_cast<int>((p.bpu + p.per_warp - 1) / p.per_warp + 1);
   p.counters_off = 256;  // [0, 256): the device error word
   p.part_off = p.counters_off + (static_cast<size_t>(p.units) * sizeof(int) + 255) / 256 * 256;
-  p.bytes = p.part_off + static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * (kD + 2) * sizeof(float);
+  p.bytes = p.part_off + static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float);
   return p;
 }
 
