@@ -68,9 +68,9 @@ int wt_set_launch_flags(int flags);
  *   y [N, 1, H*D] (element type of qkv) = softmax(q k^T / sqrt(D)) v over [gathered cache | new token].
  *   write_cache != 0: the new key/value are also written into the row's own slot offset[r] (if < C) of
  *   k_cache / v_cache (rows only read slots below their offset, so the result does not change).
- *   kv_splits: 0 = choose from the shape (wt_self_attn_step_splits); 1 = one warp per (row, head); >1 = split
+ *   kv_splits: 0 = choose from the shape (wt_self_attn_step_splits); 1 = one CTA per (row, head); >1 = split
  *   every row's cache range into that many parts combined in-kernel, which needs `workspace` of
- *   wt_self_attn_step_workspace() bytes. kv_splits must be at least ceil(capacity / 256).
+ *   wt_self_attn_step_workspace() bytes. kv_splits must be at least ceil(capacity / 1024).
  *   A workspace is laid out by the call's shape (rows, heads, head_dim, kv_splits): zero it before its first use
  *   with a shape; each call leaves its counters zeroed for the next call of the SAME shape (its partials stay as
  *   written, so another shape needs another -- or a re-zeroed -- workspace). Calls that may overlap on the GPU

@@ -89,11 +89,11 @@ def test_workspace_sizes():
 
 
 def test_split_choice():
-    """At least ceil(C / 256) parts (the staged slot-table slice), more for few rows, never below ~32 slots each."""
+    """At least ceil(C / 1024) parts (the staged slot-table slice), more for few rows, never below ~64 slots each."""
     lib = _lib.load()
     for rows, cap in ((160, 228), (320, 448), (40, 228), (5, 448), (1, 16), (1000, 4096)):
         s = lib.wt_self_attn_step_splits(rows, 20, cap, 64)
-        assert -(-cap // 256) <= s <= max(1, -(-cap // 32)), (rows, cap, s)
+        assert -(-cap // 1024) <= s <= max(1, -(-cap // 64)), (rows, cap, s)
     assert lib.wt_self_attn_step_splits(5, 20, 448, 64) > lib.wt_self_attn_step_splits(320, 20, 448, 64)
 
 

@@ -7,16 +7,18 @@
 //
 // B200 design. The step is HBM-bound (about 1 FLOP per byte) and made of many short gathers: each (row, head)
 // streams `offset` 128-byte key rows and 128-byte value rows, each from the row its slot-table entry names.
-//   * one WARP per (row, head[, key split]); the 4 warps of a CTA take 4 heads of the same row and split, so they
-//     have the same length and no warp of a CTA waits for a longer one;
-//   * the warp stages its slot-table entries in shared memory once and at once sends every key/value row of its
-//     range towards L2 (bulk prefetches: all of the range's DRAM requests in flight together), then streams 16-key
-//     stages through a 3-deep cp.async ring (16-byte copies, bypassing L1): the loads in flight hold no registers,
-//     and the ring is laid out chunk-major ([chunk][lane]) so every read-back is bank-conflict free;
-//   * a key row is covered by D/8 lanes (one 16-byte piece each); the dot product is finished with 3 butterfly
-//     shuffles; each group of D/8 lanes runs its own online softmax (4 keys per stage), merged at the end;
+//   * one CTA of 4 warps per (row, head[, key split]); the CTA stages its slot-table slice in shared memory once
+//     (so no key load waits on an index load) and its warps take 4 contiguous quarters of the keys, so the longest
+//     row's chain of dependent loads is a quarter as long as with one warp per (row, head), and the many short
+//     CTAs balance over the SMs by themselves;
+//   * each warp streams 16-key stages through a 2-deep cp.async ring (16-byte copies, bypassing L1): the loads in
+//     flight hold no registers, and the ring is laid out chunk-major ([chunk][lane]) so every read-back is bank-
+//     conflict free;
+//   * a key row is covered by D/8 lanes (one 16-byte piece each), dot products on mixed-precision FMAs (half/bf16
+//     products accumulated in fp32) finished with butterfly shuffles; each group of D/8 lanes runs its own online
+//     softmax (4 keys per stage); groups merge by shuffles, the 4 warps through shared memory;
 //   * kv_splits > 1 splits the cache capacity into equal static ranges; each split writes its partial (acc, m, l)
-//     to the workspace and the last warp of the (row, head) -- an atomic counter, no waiting -- combines them;
+//     to the workspace and the last CTA of the (row, head) -- an atomic counter, no waiting -- combines them;
 //   * with programmatic dependent launch the offset, slot table and cache reads start before the preceding kernel
 //     has finished (only the new token's q/k/v wait for it).
 #include "common.cuh"
@@ -24,11 +26,10 @@
 namespace wt {
 namespace {
 
-constexpr int kWarpsPerCta = 4;  // = heads per CTA
-constexpr int kStages = 2;       // cp.async ring depth (stages of 16 keys): the L2 prefetch covers the latency,
-                                 // a shallow ring keeps 6 CTAs (24 warps) per SM resident
+constexpr int kWarpsPerCta = 4;  // key quarters of one (row, head)
+constexpr int kStages = 2;       // cp.async ring depth per warp (stages of 16 keys)
 constexpr int kKeysPerGroup = 4;
-constexpr int kMaxSplitKeys = 256;  // keys per (row, head, split) staged in shared memory: splits >= ceil(C/256)
+constexpr int kMaxSplitKeys = 1024;  // cache slots per (row, head, split) staged in shared memory
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -104,9 +105,8 @@ __device__ __forceinline__ void merge_state(float &m, float &l, float (&acc)[8],
   m = mn;
 }
 
-// shared memory per warp: the ring ([stage][2 * 4 chunks][32 lanes] x 16 bytes), then the staged source rows
+// shared memory: per warp a ring ([stage][2 * 4 chunks][32 lanes] x 16 bytes), then the CTA's staged source rows
 constexpr int kRingBytes = kStages * 2 * kKeysPerGroup * 32 * 16;
-constexpr int kWarpSmem = kRingBytes + kMaxSplitKeys * 4;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
@@ -119,43 +119,45 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   constexpr int KPS = GPW * U;   // keys per stage
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int hgroups = (H + kWarpsPerCta - 1) / kWarpsPerCta;
-  const int r = blockIdx.x / hgroups, h = (blockIdx.x - r * hgroups) * kWarpsPerCta + warp;
+  const int r = blockIdx.x / H, h = blockIdx.x - (blockIdx.x / H) * H;
   const int sp = blockIdx.y;
-  if (h >= H) return;
   const int grp = lane / LPK, sub = lane % LPK;
   const size_t HD = static_cast<size_t>(H) * D;
-  unsigned char *ring = smem_raw + warp * kWarpSmem;
-  int *rows_s = reinterpret_cast<int *>(ring + kRingBytes);
+  unsigned char *ring = smem_raw + warp * kRingBytes;
+  int *rows_s = reinterpret_cast<int *>(smem_raw + kWarpsPerCta * kRingBytes);
 
   // Before waiting for the preceding kernel: the offset, this split's slot-table slice and the key/value rows it
   // names (inputs the kernel launched just before this one does not write; the new token's q/k/v come after).
-  // Splits are static ranges of the capacity, so the slice is known without the offset.
   const int cap = (C + splits - 1) / splits;
   const int lo = sp * cap;
   const int lim = min(C, lo + cap) - lo;
-  const int32_t *srow = src + static_cast<size_t>(r) * C + lo;
-  for (int i = lane; i < lim; i += 32) {
-    const int v = srow[i];
-    rows_s[i] = v < 0 ? 0 : (v > N - 1 ? N - 1 : v);
-  }
   const int64_t off64 = offset[r];
   const int off = static_cast<int>(off64 < 0 ? 0 : (off64 > C ? C : off64));
   const int hi = max(lo, min(off, lo + cap));  // keys [lo, hi) of this split
-  __syncwarp();
+  const int32_t *srow = src + static_cast<size_t>(r) * C + lo;
+  for (int i = threadIdx.x; i < hi - lo; i += kWarpsPerCta * 32) {
+    const int v = srow[i];
+    rows_s[i] = v < 0 ? 0 : (v > N - 1 ? N - 1 : v);
+  }
+  __syncthreads();
+  (void)lim;
 
+  // this warp's quarter: whole stages [st0, st1) of the split's range
+  const int nst_all = (hi - lo + KPS - 1) / KPS;
+  const int st0 = nst_all * warp / kWarpsPerCta, st1 = nst_all * (warp + 1) / kWarpsPerCta;
+  const int wlo = lo + st0 * KPS, whi = min(hi, lo + st1 * KPS);
+  const int nst = st1 - st0;
   const size_t row_stride = static_cast<size_t>(H) * C * D;
   const T *kh = kc + static_cast<size_t>(h) * C * D + sub * 8;
   const T *vh = vc + static_cast<size_t>(h) * C * D + sub * 8;
-  const int nst = (hi - lo + KPS - 1) / KPS;
-  // stage t: this lane's keys lo + t*KPS + grp*U + u; piece i (K: u, V: U + u) at ring[t % S][i][lane]
+  // stage t: this lane's keys wlo + t*KPS + grp*U + u; piece i (K: u, V: U + u) at ring[t % S][i][lane]
   auto issue = [&](int t) {
     unsigned char *slot = ring + (t % kStages) * (2 * U * 32 * 16);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = t * KPS + grp * U + u;  // relative to lo
-      if (j < hi - lo) {
-        const size_t o = static_cast<size_t>(rows_s[j]) * row_stride + static_cast<size_t>(lo + j) * D;
+      const int j = wlo + t * KPS + grp * U + u;
+      if (j < whi) {
+        const size_t o = static_cast<size_t>(rows_s[j - lo]) * row_stride + static_cast<size_t>(j) * D;
         cp_async16(slot + (u * 32 + lane) * 16, kh + o);
         cp_async16(slot + ((U + u) * 32 + lane) * 16, vh + o);
       }
@@ -172,28 +174,31 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   // this kernel to complete
   pdl_launch_dependents();
   const T *qrow = qkv + static_cast<size_t>(r) * 3 * HD + static_cast<size_t>(h) * D + sub * 8;
-  const uint4 qraw = ldg16(qrow), kraw = ldg16(qrow + HD), vraw = ldg16(qrow + 2 * HD);
-  if (write_cache && sp == 0 && grp == 0 && off < C) {
-    const size_t own = ((static_cast<size_t>(r) * H + h) * C + off) * D + sub * 8;
-    *reinterpret_cast<uint4 *>(kc + own) = kraw;
-    *reinterpret_cast<uint4 *>(vc + own) = vraw;
-  }
+  const uint4 qraw = ldg16(qrow);
   const uint32_t qw[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
-  float s_new = 0.f;
-  s_new = MixFma<T>::dot2(qw[0], kraw.x, s_new);
-  s_new = MixFma<T>::dot2(qw[1], kraw.y, s_new);
-  s_new = MixFma<T>::dot2(qw[2], kraw.z, s_new);
-  s_new = MixFma<T>::dot2(qw[3], kraw.w, s_new);
-  s_new = group_sum<LPK>(s_new) * scale;  // (the scale after the dot product, as attn_plugin.py:332)
-  // the new token first: every row attends to it (attn_plugin.py:331-334); group 0 of split 0 owns it
+  // the new token first: every row attends to it (attn_plugin.py:331-334); group 0 of warp 0 of split 0 owns it
+  const bool owner = sp == 0 && warp == 0;
   float m = kNegInf, l = 0.f, acc[8];
-  if (sp == 0 && grp == 0) {
-    m = s_new;
-    l = 1.f;
-    unpack8<T>(vraw, acc);
-  } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  if (owner) {
+    const uint4 kraw = ldg16(qrow + HD), vraw = ldg16(qrow + 2 * HD);
+    if (write_cache && grp == 0 && off < C) {
+      const size_t own = ((static_cast<size_t>(r) * H + h) * C + off) * D + sub * 8;
+      *reinterpret_cast<uint4 *>(kc + own) = kraw;
+      *reinterpret_cast<uint4 *>(vc + own) = vraw;
+    }
+    float s_new = 0.f;
+    s_new = MixFma<T>::dot2(qw[0], kraw.x, s_new);
+    s_new = MixFma<T>::dot2(qw[1], kraw.y, s_new);
+    s_new = MixFma<T>::dot2(qw[2], kraw.z, s_new);
+    s_new = MixFma<T>::dot2(qw[3], kraw.w, s_new);
+    s_new = group_sum<LPK>(s_new) * scale;  // (the scale after the dot product, as attn_plugin.py:332)
+    if (grp == 0) {
+      m = s_new;
+      l = 1.f;
+      unpack8<T>(vraw, acc);
+    }
   }
 
   for (int t = 0; t < nst; ++t) {
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     bool ok[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      ok[u] = t * KPS + grp * U + u < hi - lo;
+      ok[u] = wlo + t * KPS + grp * U + u < whi;
       const uint4 kw = *reinterpret_cast<const uint4 *>(slot + (u * 32 + lane) * 16);
       float a = 0.f;
       a = MixFma<T>::dot2(qw[0], kw.x, a);
@@ -243,7 +248,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   }
   cp_async_wait<0>();
 
-  // merge the lane groups of the warp
+  // merge the lane groups of the warp, then the warps of the CTA (through shared memory: the rings are done)
 #pragma unroll
   for (int o = LPK; o < 32; o <<= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
@@ -252,55 +257,69 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     for (int i = 0; i < 8; ++i) acc2[i] = __shfl_xor_sync(0xffffffffu, acc[i], o);
     merge_state(m, l, acc, m2, l2, acc2);
   }
+  __syncthreads();
+  float *st_s = reinterpret_cast<float *>(smem_raw);  // [warp][D + 2]
+  if (grp == 0) {
+    float *mine = st_s + warp * (D + 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mine[sub * 8 + i] = acc[i];
+    if (sub == 0) {
+      mine[D] = m;
+      mine[D + 1] = l;
+    }
+  }
+  __syncthreads();
+  if (warp != 0 || grp != 0) return;
+#pragma unroll
+  for (int w2 = 1; w2 < kWarpsPerCta; ++w2) {
+    const float *other = st_s + w2 * (D + 2);
+    float acc2[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc2[i] = other[sub * 8 + i];
+    merge_state(m, l, acc, other[D], other[D + 1], acc2);
+  }
   const int rh = r * H + h;
   T *yo = y + static_cast<size_t>(r) * HD + static_cast<size_t>(h) * D + sub * 8;
   if (splits == 1) {
-    if (grp == 0) {
-      const float inv = 1.f / l;
+    const float inv = 1.f / l;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] *= inv;
-      *reinterpret_cast<uint4 *>(yo) = pack8<T>(acc);
-    }
+    for (int i = 0; i < 8; ++i) acc[i] *= inv;
+    *reinterpret_cast<uint4 *>(yo) = pack8<T>(acc);
     return;
   }
-  // the last split of this (row, head) to finish combines the partials
+  // the last split of this (row, head) to finish combines the partials (lanes 0 .. LPK-1 of warp 0)
   float *pp = part + (static_cast<size_t>(rh) * splits + sp) * (D + 2);
-  if (grp == 0) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pp[sub * 8 + i] = acc[i];
-    if (sub == 0) {
-      pp[D] = m;
-      pp[D + 1] = l;
-    }
+  for (int i = 0; i < 8; ++i) pp[sub * 8 + i] = acc[i];
+  if (sub == 0) {
+    pp[D] = m;
+    pp[D + 1] = l;
   }
   __threadfence();
-  __syncwarp();
+  __syncwarp((1u << LPK) - 1);
   int last = 0;
-  if (lane == 0) last = (atomicAdd(counters + rh, 1) == splits - 1);
-  last = __shfl_sync(0xffffffffu, last, 0);
+  if (sub == 0) last = (atomicAdd(counters + rh, 1) == splits - 1);
+  last = __shfl_sync((1u << LPK) - 1, last, 0);
   if (!last) return;
   __threadfence();
-  if (grp == 0) {
-    const float *pr = part + static_cast<size_t>(rh) * splits * (D + 2);
-    float top = kNegInf;
-    for (int s2 = 0; s2 < splits; ++s2) top = fmaxf(top, __ldcg(pr + s2 * (D + 2) + D));
-    float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
-    for (int s2 = 0; s2 < splits; ++s2) {
-      const float *p2 = pr + s2 * (D + 2);
-      const float ms = __ldcg(p2 + D);
-      const float wgt = (ms == kNegInf) ? 0.f : ex2(ms - top);
-      den = fmaf(wgt, __ldcg(p2 + D + 1), den);
+  const float *pr = part + static_cast<size_t>(rh) * splits * (D + 2);
+  float top = kNegInf;
+  for (int s2 = 0; s2 < splits; ++s2) top = fmaxf(top, __ldcg(pr + s2 * (D + 2) + D));
+  float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
+  for (int s2 = 0; s2 < splits; ++s2) {
+    const float *p2 = pr + s2 * (D + 2);
+    const float ms = __ldcg(p2 + D);
+    const float wgt = (ms == kNegInf) ? 0.f : ex2(ms - top);
+    den = fmaf(wgt, __ldcg(p2 + D + 1), den);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(p2 + sub * 8 + i), num[i]);
-    }
-    const float inv = 1.f / den;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) num[i] *= inv;
-    *reinterpret_cast<uint4 *>(yo) = pack8<T>(num);
+    for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(p2 + sub * 8 + i), num[i]);
   }
-  if (lane == 0) counters[rh] = 0;  // left zeroed for the next launch
+  const float inv = 1.f / den;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) num[i] *= inv;
+  *reinterpret_cast<uint4 *>(yo) = pack8<T>(num);
+  if (sub == 0) counters[rh] = 0;  // left zeroed for the next launch
 }
-
 
 size_t step_workspace(int rows, int heads, int head_dim, int splits) {
   if (splits <= 1) return 0;
@@ -311,12 +330,13 @@ size_t step_workspace(int rows, int heads, int head_dim, int splits) {
 template <typename T, int D>
 int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y, int N,
                 int H, int C, int write_cache, int splits, void *ws, void *stream) {
-  constexpr int smem = kWarpsPerCta * kWarpSmem;
+  const int cap = (C + splits - 1) / splits;
+  const int smem = kWarpsPerCta * kRingBytes + (cap * 4 + 15) / 16 * 16;
   auto kernel = self_step_kernel<T, D>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static int attr_bytes = 0;
+  if (smem > attr_bytes) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_set = true;
+    attr_bytes = smem;
   }
   int *counters = nullptr;
   float *part = nullptr;
@@ -326,8 +346,8 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
                                      (static_cast<size_t>(N) * H * sizeof(int) + 255) / 256 * 256);
   }
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(D)) * 1.4426950408889634);
-  const int hgroups = (H + kWarpsPerCta - 1) / kWarpsPerCta;
-  return launch("self_attn_step", kernel, dim3(N * hgroups, splits), dim3(kWarpsPerCta * 32), smem, stream, static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
+  return launch("self_attn_step", kernel, dim3(N * H, splits), dim3(kWarpsPerCta * 32), smem, stream,
+                static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
                 static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale);
 }
 
@@ -348,14 +368,16 @@ int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *off
 
 extern "C" {
 
+static constexpr int kMaxSplitKeysPublic = wt::kMaxSplitKeys;
+
 int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim) {
-  // one warp per (row, head, split), at most 256 slots each; split further only when the (row, head) pairs alone
-  // would leave the SMs short of warps (< 4 per SM): measured, splitting costs more than it hides otherwise
+  // one CTA of 4 warps per (row, head, split), at most 1024 slots each; split further only when the (row, head)
+  // pairs alone would leave the SMs short of CTAs (< 2 per SM): splitting costs a partial and a combine
   const long long items = static_cast<long long>(rows) * heads;
-  long long s = (capacity + 255) / 256;
-  const long long want = (148LL * 4 + items - 1) / items;
+  long long s = (capacity + kMaxSplitKeysPublic - 1) / kMaxSplitKeysPublic;
+  const long long want = (148LL * 2 + items - 1) / items;
   if (want > s) s = want;
-  const long long cap = (capacity + 31) / 32;  // at least ~32 keys per split
+  const long long cap = (capacity + 63) / 64;  // at least ~64 keys (16 per warp) per split
   if (s > cap) s = cap;
   if (s < 1) s = 1;
   if (s > 64) s = 64;
@@ -381,8 +403,7 @@ int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, 
   WT_ALIGNED(offset);
   WT_ALIGNED(src);
   WT_ALIGNED(y);
-  WT_REQUIRE(static_cast<long long>(rows) * ((heads + kWarpsPerCta - 1) / kWarpsPerCta) < (1LL << 31), WT_ERR_ARG,
-             "self_attn_step: rows*heads too large");
+  WT_REQUIRE(static_cast<long long>(rows) * heads < (1LL << 31), WT_ERR_ARG, "self_attn_step: rows*heads too large");
   int splits = kv_splits > 0 ? kv_splits : wt_self_attn_step_splits(rows, heads, capacity, head_dim);
   if (splits > capacity) splits = capacity;
   WT_REQUIRE(splits <= 65535, WT_ERR_ARG, "self_attn_step: kv_splits %d too large", splits);

@@ -95,7 +95,7 @@ def _qk_scale(d: int) -> float:
 # --- self-attention ----------------------------------------------------------------------------------------
 def self_attn_step_config(rows: int, heads: int = 20, capacity: int = 448, head_dim: int = 64) -> tuple[int, int]:
     """(key splits per (row, head), warps per CTA) this build launches for ``rows`` rows -- the counterpart of the
-    reference's (keys per block, warps) choice (attn_plugin.py:482-485)."""
+    reference's (keys per block, warps) choice (attn_plugin.py:482-485). A CTA's 4 warps split its keys."""
     return int(_lib.load().wt_self_attn_step_splits(rows, heads, capacity, head_dim)), 4
 
 
@@ -107,7 +107,7 @@ def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     caches at ``offset`` (in place). Reference: attn_plugin.py:488-501 (kernel :309-350).
 
     ``config`` is accepted for call-compatibility and ignored; ``kv_splits`` (None: chosen from the shape) splits
-    every row's cache into that many parts (at least ceil(C / 256))."""
+    every row's cache into that many parts (at least ceil(C / 1024))."""
     what = "self_attn_step"
     if qkv.dim() != 3:
         raise ValueError(f"{what}: qkv must be [N, S, 3*H*D]")
@@ -132,7 +132,7 @@ def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
         raise ValueError(f"{what}: out must be [N, 1, H*D] of qkv's dtype")
     lib = _lib.load()
     splits = int(kv_splits) if kv_splits else int(lib.wt_self_attn_step_splits(n, h, c, d))
-    splits = max(splits, -(-c // 256))  # (at most 256 cache slots per split)
+    splits = max(splits, -(-c // 1024))  # (at most 1024 cache slots per split)
     ws_ptr, ws_bytes = None, 0
     if splits > 1:
         ws_bytes = int(lib.wt_self_attn_step_workspace(n, h, d, splits))
