@@ -30,7 +30,9 @@ constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
 constexpr int kErrTimeout = 1;
 constexpr int kPart = kD + 4;  // floats per query of a partial: acc[64], m, l, 2 pad (16-byte aligned records)
 
-// Launch shapes: warps per CTA (one CTA per SM) x ring stages per warp. Shared memory: warps * stages * 4 KB.
+// Launch shapes: warps per CTA x ring stages per warp x CTAs per SM. Shared memory: warps * stages * 4 KB per CTA.
+// Default: 6 warps x 4 stages, 2 CTAs per SM (measured best at 8 and 32 windows; 4x6, 3x8, 5x5 x 2 CTAs and
+// 12x4 x 1 CTA were slower).
 struct Shape {
   int warps, stages;
   bool pair;  // two 16-key blocks per step of the online softmax
@@ -434,19 +436,23 @@ int launch_stream_shape(const CUtensorMap &km, const CUtensorMap &vm, const Stre
 template <typename T, int NT>
 int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamArgs &a, int grid, int shape,
                      void *stream) {
-  switch (shape) {
+  if constexpr (NT >= 2) {  // (more query tiles: shape 0 only)
+    return launch_stream_shape<T, NT, kShapes[0].warps, kShapes[0].stages, kShapes[0].pair>(km, vm, a, grid, stream);
+  } else {
+    switch (shape) {
 #define WT_SHAPE_CASE(i)                                                                                      \
   case i:                                                                                                    \
     return launch_stream_shape<T, NT, kShapes[i].warps, kShapes[i].stages, kShapes[i].pair>(km, vm, a, grid, \
                                                                                              stream);
-    WT_SHAPE_CASE(0)
-    WT_SHAPE_CASE(1)
-    WT_SHAPE_CASE(2)
-    WT_SHAPE_CASE(3)
-    default:
-      return launch_stream_shape<T, NT, kShapes[4].warps, kShapes[4].stages, kShapes[4].pair>(km, vm, a, grid,
-                                                                                             stream);
+      WT_SHAPE_CASE(0)
+      WT_SHAPE_CASE(1)
+      WT_SHAPE_CASE(3)
+      WT_SHAPE_CASE(4)
 #undef WT_SHAPE_CASE
+      default:
+        return launch_stream_shape<T, NT, kShapes[2].warps, kShapes[2].stages, kShapes[2].pair>(km, vm, a, grid,
+                                                                                               stream);
+    }
   }
 }
 
