@@ -308,7 +308,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     ker = kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src)
 
     # end to end through the public API: H2D of the step's inputs from pinned memory, the step, D2H of its outputs
-    e2e = run_e2e(torch, graph, dev, qkv, q, y_self, y_cross, args.steps, reset_state, sch, args.warmup)
+    e2e = run_e2e(torch, graph, dev, qkv, q, y_self, y_cross, args.steps, reset_state, sch, args.warmup, dist)
 
     peak, peak_kind = measured_hbm_peak()
     cross_bytes = sch.cross_launch_bytes()
@@ -393,7 +393,9 @@ def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, 
     return {"self_ms": self_ms, "cross_ms": cross_ms, "self_bytes": self_bytes}
 
 
-def run_e2e(torch, graph, dev, qkv, q, y_self, y_cross, steps, reset_state, sch, warmup) -> dict:
+def run_e2e(torch, graph, dev, qkv, q, y_self, y_cross, steps, reset_state, sch, warmup, dist=None) -> dict:
+    """The step through the public API with its inputs copied in from pinned host memory and its outputs copied
+    out, the host waiting for each step's result; whole-job GB/s (bytes summed over ranks, time the max)."""
     qkv_h = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
     q_h = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     qkv_h.copy_(qkv)
@@ -404,6 +406,9 @@ def run_e2e(torch, graph, dev, qkv, q, y_self, y_cross, steps, reset_state, sch,
     stream = torch.cuda.current_stream(dev)
     for _ in range(warmup):
         graph.replay()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
@@ -416,8 +421,8 @@ def run_e2e(torch, graph, dev, qkv, q, y_self, y_cross, steps, reset_state, sch,
         stream.synchronize()  # the host reads the step's result
     ev1.record()
     torch.cuda.synchronize(dev)
-    ms = ev0.elapsed_time(ev1)
-    nbytes = sum(sch.step_bytes(s) for s in range(warmup, warmup + steps))
+    ms, nbytes = combine_ranks(ev0.elapsed_time(ev1), sum(sch.step_bytes(s) for s in range(warmup, warmup + steps)),
+                               dist, dev)
     h2d = qkv.numel() * qkv.element_size() + q.numel() * q.element_size()
     d2h = y_self.numel() * y_self.element_size() + y_cross.numel() * y_cross.element_size()
     return {"value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 4),

@@ -170,6 +170,27 @@ int wt_beam_update(const float *top_s, const int64_t *top_i, int64_t *t, int64_t
 int wt_slot_reset(int32_t *src, const int64_t *slots, int n_slots, int windows, int beams, int capacity,
                   int prefilled, void *stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * The scoring half of a beam step, feeding wt_beam_update.
+ * Replaces beam_kernels.py:351-361 scores() (kernel :36-135 _scores_kernel, beam mode) and the topk of
+ * search.py:253 (PyTorch path: search.py:283-289 _choose, :313-338 _timestamp_rules, :369-371, :259-260):
+ *   per row r of window b = r / beams: the logits [N, V] fp32 with the suppressed tokens (suppress [V], 0/1 bytes)
+ *   and, at the window's first step (t[b] == 0), the begin-suppressed ones (begin [V]) set to the lowest float;
+ *   with `timestamps`, CTranslate2's timestamp rules on the row's history hist [N, hist_len] (max_initial [1]);
+ *   scores = log_softmax(masked) + cum[r] -> `scores` [N, V] (may be NULL: not written);
+ *   ns [B] = exp(logit[no_speech] - logsumexp(logits)) of each window's first row;
+ *   top_s / top_i [B, 2*beams]: the window's best 2K of its beams x V candidate scores, best first, equal scores
+ *   in index order; top_i = beam * V + token. Up to 8 beams; beams * vocab < 2^31.
+ *   Needs a workspace of wt_beam_scores_workspace() bytes, zeroed before first use (left zeroed by each call);
+ *   calls that may overlap on the GPU must not share one.
+ * ------------------------------------------------------------------------------------------------------- */
+size_t wt_beam_scores_workspace(int windows, int beams);
+int wt_beam_scores(const float *logits, const uint8_t *suppress, const uint8_t *begin, const int64_t *t,
+                   const float *cum, const int64_t *hist, const int64_t *max_initial, float *scores, float *ns,
+                   float *top_s, int64_t *top_i, int windows, int beams, int vocab, int hist_len, int timestamps,
+                   int no_speech, int no_timestamps, int ts_begin, int eot, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -159,3 +159,78 @@ def beam_update(st: dict, top_s: np.ndarray, top_i: np.ndarray, ns: np.ndarray, 
             st["pos"][b] = pb + 1
             st["t"][b] = tb + 1
     assert S >= 1
+
+
+LOWEST = np.float32(np.finfo(np.float32).min)
+
+
+def beam_scores(logits: np.ndarray, suppress: np.ndarray, begin: np.ndarray, t: np.ndarray, cum: np.ndarray,
+                hist: np.ndarray, max_initial: int, K: int, timestamps: bool, no_speech: int, no_timestamps: int,
+                ts_begin: int, eot: int):
+    """The candidate scores of a beam step: search.py:283-289 ``_choose`` (suppressed tokens, at a window's first
+    step the begin-suppressed ones, set to the lowest float), with ``timestamps`` search.py:313-338
+    ``_timestamp_rules`` (CTranslate2's ApplyTimestampRules), log-softmax, plus the row's cumulative
+    log-probability (search.py:370); and each window's no-speech probability from its first row's raw logits
+    (search.py:259-260). The fused form of the same is beam_kernels.py:36-135 ``_scores_kernel``.
+
+    logits [N, V] f32; suppress/begin [V] bool; t [B] int64; cum [N] f32; hist [N, T] int64.
+    Returns (scores [N, V] f32, ns [B] f32)."""
+    n, v = logits.shape
+    x = logits.astype(np.float32).copy()
+    B = n // K
+    tr = np.repeat(np.asarray(t, dtype=np.int64), K)  # [N]
+    first = tr == 0
+    x[np.broadcast_to(suppress[None, :], x.shape)] = LOWEST
+    x[np.outer(first, begin)] = LOWEST
+    if timestamps:
+        tb = ts_begin
+        ids = np.arange(v)
+        g = np.maximum(tr, 0)
+        first_ts = g == 0
+        rows = np.arange(n)
+        last = hist[rows, np.maximum(g - 1, 0)]
+        pen = np.where(g >= 2, hist[rows, np.maximum(g - 2, 0)], last)
+        last_ts, pen_ts = last >= tb, pen >= tb
+        T = hist.shape[1]
+        is_ts = (hist >= tb) & (np.arange(T)[None, :] < g[:, None])
+        at = np.where(is_ts, np.arange(T)[None, :], -1).max(1)
+        latest = hist[rows, np.maximum(at, 0)]
+        mask = (ids[None, :] == no_timestamps) | (first_ts[:, None] & ((ids[None, :] < tb)
+                                                                        | (ids[None, :] > tb + max_initial)))
+        mask |= (~first_ts & last_ts & pen_ts)[:, None] & (ids[None, :] >= tb)
+        pair = ~first_ts & last_ts & ~pen_ts
+        mask |= pair[:, None] & ((ids[None, :] < eot) | ((ids[None, :] >= tb) & (ids[None, :] < last[:, None])))
+        mask |= (~first_ts & ~last_ts & (at >= 0))[:, None] & (ids[None, :] >= tb) & (ids[None, :] <= latest[:, None])
+        x[mask] = LOWEST
+        lp = _log_softmax(x)
+        with np.errstate(divide="ignore"):
+            ts_lse = _logsumexp(lp[:, tb:])
+        sample_ts = ts_lse > lp[:, :tb].max(-1)
+        check = pair | (~first_ts & ~last_ts)
+        x[(check & sample_ts)[:, None] & (ids[None, :] < tb)] = LOWEST
+    scores = (_log_softmax(x) + np.asarray(cum, dtype=np.float32)[:, None]).astype(np.float32)
+    lg = logits[::K].astype(np.float64)
+    ns = np.exp(lg[:, no_speech] - _logsumexp(lg)).astype(np.float32)
+    assert ns.shape == (B,)
+    return scores, ns
+
+
+def _logsumexp(x: np.ndarray) -> np.ndarray:
+    x = x.astype(np.float64)
+    m = x.max(-1)
+    return m + np.log(np.exp(x - m[:, None]).sum(-1))
+
+
+def _log_softmax(x: np.ndarray) -> np.ndarray:
+    x64 = x.astype(np.float64)
+    return (x64 - _logsumexp(x64)[:, None]).astype(np.float32)
+
+
+def beam_topk(scores: np.ndarray, K: int):
+    """The best 2K of each window's K x V candidate scores (search.py:371 ``topk(2 * K)``), best first; equal
+    scores in index order. Returns (top_s [B, 2K] f32, top_i [B, 2K] int64 = beam * V + token)."""
+    n, v = scores.shape
+    flat = scores.reshape(n // K, K * v)
+    order = np.lexsort((np.arange(K * v)[None, :].repeat(flat.shape[0], 0), -flat.astype(np.float64)), axis=1)
+    top_i = order[:, : 2 * K].astype(np.int64)
+    return np.take_along_axis(flat, top_i, 1).astype(np.float32), top_i

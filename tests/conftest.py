@@ -28,6 +28,13 @@ def attn_golden():
 
 
 @pytest.fixture(scope="session")
+def scores_golden():
+    import numpy as np
+
+    return np.load(ROOT / "tests" / "golden" / "scores_golden.npz")
+
+
+@pytest.fixture(scope="session")
 def slots_golden():
     import numpy as np
 

@@ -143,6 +143,104 @@ def slots_golden(ref_src: str) -> dict:
     return out
 
 
+# --- the beam step's candidate scores: masks, timestamp rules, log-softmax + cum, top-2K (reference Search) ------
+TS_V, TS_NOTS, TS_TSB = 120, 40, 41  # toy vocabulary with timestamps: text 4..39, <|notimestamps|> 40, 41.. times
+
+
+def _ts_logits(history, seed):
+    """Pseudo-random logits of a history that keep every timestamp rule busy: the timestamps just after the
+    latest one are favoured, the rest disfavoured, and EOS grows likelier with length."""
+    g = torch.Generator().manual_seed(zlib.crc32(repr(("ts-golden", seed, history)).encode()))
+    x = torch.randn(TS_V, generator=g, dtype=torch.float64) * 2.5
+    x[EOT] += 0.2 * len(history)
+    latest = max([h - TS_TSB for h in history if h >= TS_TSB], default=-1)
+    near = torch.arange(TS_V - TS_TSB)
+    x[TS_TSB:] += torch.where((near > latest) & (near <= latest + 5), 2.0, -1.0).double()
+    return x
+
+
+def _fake_step_with(logits_of, seed):
+    def step_fn(tokens, offset, cache, logits, new_kv, src):
+        def run():
+            for n in range(tokens.shape[0]):
+                off = int(offset[n])
+                hist = [int(round(float(cache[0, 0, int(src[n, j]), 0, j, 0]))) for j in range(off)]
+                for s in range(tokens.shape[1]):
+                    tok = int(tokens[n, s])
+                    logits[n, s] = logits_of(hist + [tok], seed).float()
+                    new_kv[0, :, n, 0, s, :] = float(tok)
+                    hist.append(tok)
+
+        return run
+
+    return step_fn
+
+
+def scores_golden(ref_src: str) -> dict:
+    """Per beam step of the reference Search (PyTorch path, CPU): its inputs (logits, t, cum, hist) and its
+    candidate scores (log-softmax of the masked logits + cum), best 2K and no-speech probabilities; two decodes
+    without timestamps (V 40, beam 3 / 5) and two with CTranslate2's timestamp rules (V 120, beam 3 / 4)."""
+    from whisper_trt.config import WhisperConfig
+    from whisper_trt.search import Search
+
+    out = {}
+    step_no = 0
+    runs = [(3, 10, False), (5, 11, False), (3, 12, True), (4, 13, True)]
+    for run, (K, seed, ts) in enumerate(runs):
+        if ts:
+            cfg = WhisperConfig(n_mels=4, d_model=4, enc_layers=1, enc_heads=1, enc_ffn=4, dec_layers=1,
+                                dec_heads=1, dec_ffn=4, vocab_size=TS_V, eot=EOT, sot=SOT, no_speech=NOSPEECH,
+                                no_timestamps=TS_NOTS, timestamp_begin=TS_TSB)
+            fake, vocab = _fake_step_with(_ts_logits, seed), TS_V
+            prompts = [[SOT, 10 + w, 20 + w % 3] for w in range(5)]
+        else:
+            cfg = WhisperConfig(n_mels=4, d_model=4, enc_layers=1, enc_heads=1, enc_ffn=4, dec_layers=1,
+                                dec_heads=1, dec_ffn=4, vocab_size=V, eot=EOT, sot=SOT, no_speech=NOSPEECH)
+            fake, vocab = _fake_step_with(_scores_of, seed), V
+            prompts = [[SOT, 10 + w, 20 + w % 3, 30] for w in range(5)]
+        W = 2
+        search = Search(cfg, fake, W, K, len(prompts[0]), "beam", dtype=torch.float32, device="cpu",
+                        max_length=40 if not ts else 36, graphs=False, fused=False, timestamps=ts)
+        rec = {}
+        orig_choose, orig_beam = search._choose, search._beam
+
+        def choose(logits, s=search, orig=orig_choose, rec=rec):
+            rec.clear()
+            rec["logits"] = logits.clone()
+            rec["t"], rec["cum"], rec["hist"] = s.t.clone(), s.cum.clone(), s.hist.clone()
+            orig(logits)
+
+        def beam(logp, prompt, s=search, orig=orig_beam, rec=rec):
+            nonlocal step_no
+            sc = logp + s.cum[:, None]
+            top_s, top_i = sc.view(s.B, -1).topk(2 * s.K, dim=1)
+            lg = rec["logits"][:: s.K]
+            ns = (lg[:, s.cfg.no_speech] - lg.logsumexp(-1)).exp()
+            key = f"step{step_no:04d}"
+            out[f"{key}/logits"] = rec["logits"].numpy()
+            out[f"{key}/t"] = rec["t"].numpy()
+            out[f"{key}/cum"] = rec["cum"].numpy()
+            out[f"{key}/hist"] = rec["hist"].numpy()
+            out[f"{key}/scores"] = sc.numpy()
+            out[f"{key}/top_s"] = top_s.numpy()
+            out[f"{key}/top_i"] = top_i.numpy()
+            out[f"{key}/ns"] = ns.numpy()
+            out[f"{key}/suppress"] = s.suppress.numpy()
+            out[f"{key}/begin"] = s.begin.numpy()
+            out[f"{key}/meta"] = np.array([K, vocab, int(ts), int(s.max_initial[0]), s.cfg.no_speech,
+                                           s.cfg.no_timestamps or 0, s.cfg.timestamp_begin or 0, s.cfg.eot, run],
+                                          dtype=np.int64)
+            step_no += 1
+            orig(logp, prompt)
+
+        search._choose = choose
+        search._beam = beam
+        suppress, begin = [5, 6, 7], [8, EOT]
+        search.stream(prompts, lambda slots, windows: None, suppress, begin, check_every=1, ahead=1,
+                      **({"max_initial_timestamp_index": 10} if ts else {}))
+    return out
+
+
 def main() -> None:
     ap_ = argparse.ArgumentParser()
     ap_.add_argument("--reference-src", default="/root/reference/src")
@@ -156,7 +254,10 @@ def main() -> None:
     np.savez_compressed(HERE / "attn_golden.npz", **a)
     s = slots_golden(args.reference_src)
     np.savez_compressed(HERE / "slots_golden.npz", **s)
-    print(f"attn cases: {len(cases.ATTN_CASES)}; bookkeeping steps: {sum(k.endswith('/meta') for k in s)}")
+    sc = scores_golden(args.reference_src)
+    np.savez_compressed(HERE / "scores_golden.npz", **sc)
+    print(f"attn cases: {len(cases.ATTN_CASES)}; bookkeeping steps: {sum(k.endswith('/meta') for k in s)}; "
+          f"scoring steps: {sum(k.endswith('/meta') for k in sc)}")
 
 
 if __name__ == "__main__":

@@ -64,6 +64,12 @@ def test_bad_arguments_return_status_without_a_gpu():
     assert st == _lib.WT_ERR_WORKSPACE
     st = lib.wt_cross_attn(0, p, p, p, p, 2, 5, 20, 1500, 64, None, 0, None)
     assert st == _lib.WT_ERR_WORKSPACE
+    st = lib.wt_beam_scores(*([p] * 11), 2, 5, 51866, 16, 0, 50362, 0, 0, 50257, None, 0, None)
+    assert st == _lib.WT_ERR_WORKSPACE
+    st = lib.wt_beam_scores(*([p] * 11), 2, 9, 51866, 16, 0, 50362, 0, 0, 50257, p, 1 << 20, None)
+    assert st == _lib.WT_ERR_UNSUPPORTED  # more than 8 beams
+    st = lib.wt_beam_scores(*([p] * 11), 2, 5, 51866, 16, 1, 50362, 50363, 0, 50257, p, 1 << 20, None)
+    assert st == _lib.WT_ERR_ARG  # timestamps without a timestamp_begin
     st = lib.wt_self_attn(0, p, p, p, p, p, p, 4, 0, 20, 96, 64, None)
     assert st == _lib.WT_ERR_ARG and b"sizes" in lib.wt_last_error()
     st = lib.wt_self_attn(0, p, p, p, p, p, p + 8, 4, 3, 20, 96, 64, None)

@@ -157,3 +157,37 @@ def test_slot_reset():
     assert (src[3:6] == 7).all()
     osl.slot_reset(src, np.array([1]), 3, prefilled=True)
     assert (src[3:6] == 3).all()
+
+
+def _score_steps(z):
+    return sorted({k.split("/")[0] for k in z.files})
+
+
+def score_inputs(z, key):
+    K, V, ts, mi, ns_id, nots, tsb, eot, _ = z[f"{key}/meta"].tolist()
+    return dict(logits=z[f"{key}/logits"], suppress=z[f"{key}/suppress"], begin=z[f"{key}/begin"], t=z[f"{key}/t"],
+                cum=z[f"{key}/cum"], hist=z[f"{key}/hist"], max_initial=mi, K=K, timestamps=bool(ts),
+                no_speech=ns_id, no_timestamps=nots, ts_begin=tsb, eot=eot)
+
+
+def test_beam_scores_match_reference(scores_golden):
+    """The candidate scores (masks, timestamp rules, log-softmax + cum) and no-speech probabilities of 191 beam
+    steps of the reference Search (with and without timestamps) from the oracle restatement: finite scores within
+    1e-5, the same masked entries, the same best 2K (none of them tied: the fixture's decodes keep 2K allowed
+    tokens at every step)."""
+    text_masked = 0
+    for key in _score_steps(scores_golden):
+        inp = score_inputs(scores_golden, key)
+        sc, ns = osl.beam_scores(**inp)
+        ref = scores_golden[f"{key}/scores"]
+        fin = ref > -1e30
+        assert np.array_equal(sc > -1e30, fin), key
+        assert np.abs(sc[fin] - ref[fin]).max() < 1e-5, key
+        assert np.abs(ns - scores_golden[f"{key}/ns"]).max() < 1e-6, key
+        top_s, top_i = osl.beam_topk(sc, inp["K"])
+        assert np.array_equal(top_i, scores_golden[f"{key}/top_i"]), key
+        assert np.allclose(top_s, scores_golden[f"{key}/top_s"], atol=1e-5, rtol=0), key
+        if inp["timestamps"]:
+            tsb = inp["ts_begin"]
+            text_masked += int(((ref[:, :tsb] < -1e30).all(1) & fin[:, tsb:].any(1)).sum())
+    assert text_masked > 50  # the timestamp probability check fired (text masked in favour of timestamps)

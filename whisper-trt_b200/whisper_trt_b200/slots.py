@@ -8,7 +8,13 @@ kernels (``wt_beam_reorder``, ``wt_beam_update``, ``wt_slot_reset``); integer wo
 * :func:`update` -- a drop-in for the reference's ``beam_kernels.update(s, top_s, top_i, ns)``
   (beam_kernels.py:292-302, kernel :169-269) in beam mode: CTranslate2's candidate rules, hypotheses, the new
   beams' histories / tables / scores / tokens, prompt feeding, advancing;
-* :func:`slot_reset` -- a window loaded into slots (search.py:440-446).
+* :func:`slot_reset` -- a window loaded into slots (search.py:440-446);
+* :func:`scores` / :func:`best` -- the scoring half of the step: masked log-softmax + cumulative score (with
+  CTranslate2's timestamp rules when ``s.timestamps``), no-speech probabilities and each window's best 2K
+  candidates in one kernel (``wt_beam_scores``): the reference's beam_kernels.scores (beam_kernels.py:351-361,
+  kernel :36-135) and the torch.topk after it (search.py:253);
+* :func:`step_bookkeeping` -- scores, best 2K and update: the fused branch of the reference's Search._body
+  (search.py:251-256) in two kernels.
 """
 
 from __future__ import annotations
@@ -16,6 +22,21 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+
+
+_workspaces: dict[tuple, torch.Tensor] = {}
+
+
+def _workspace(dev: torch.device, key: tuple, nbytes: int) -> torch.Tensor:
+    k = (dev.index if dev.index is not None else torch.cuda.current_device(),) + key
+    ws = _workspaces.get(k)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"beam_scores workspace of {nbytes} bytes needed during CUDA-graph capture: run the "
+                               "call once before capturing")
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        _workspaces[k] = ws
+    return ws
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -112,3 +133,58 @@ def slot_reset(src: torch.Tensor, slots: torch.Tensor, K: int, prefilled: bool) 
         st = _lib.load().wt_slot_reset(src.data_ptr(), slots.data_ptr(), slots.numel(), n // K, K, c, int(prefilled),
                                        torch.cuda.current_stream(dev).cuda_stream)
     _lib.check(st, what)
+
+
+def best(s, logits: torch.Tensor, ns: torch.Tensor, out: torch.Tensor | None = None,
+         top: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Each window's best 2K candidates (top_s [B, 2K] float32, top_i [B, 2K] int64 = beam * V + token, best
+    first) of the scores log_softmax(masked logits) + cum; ``ns`` [B] gets the no-speech probabilities and ``out``
+    [N, V] (optional) the scores themselves. ``s`` is a search state with the reference Search's buffers (beam
+    mode): suppress / begin [V] bool, t [B], cum [N], hist [N, T], max_initial [1], K, cfg, timestamps."""
+    what = "beam_scores"
+    B, K = s.t.shape[0], s.K
+    n, v = logits.shape
+    if n != B * K:
+        raise ValueError(f"{what}: logits has {n} rows, expected {B} x {K}")
+    _need(what, logits, torch.float32)
+    _need(what, ns, torch.float32, (B,))
+    if out is not None:
+        _need(what, out, torch.float32, (n, v))
+    for name, dt, shape in (("suppress", torch.bool, (v,)), ("begin", torch.bool, (v,)), ("t", torch.int64, (B,)),
+                            ("cum", torch.float32, (n,)), ("hist", torch.int64, None),
+                            ("max_initial", torch.int64, (1,))):
+        _need(f"{what}.{name}", getattr(s, name), dt, shape)
+    if top is None:
+        top = (torch.empty(B, 2 * K, dtype=torch.float32, device=logits.device),
+               torch.empty(B, 2 * K, dtype=torch.int64, device=logits.device))
+    top_s, top_i = top
+    _need(what, top_s, torch.float32, (B, 2 * K))
+    _need(what, top_i, torch.int64, (B, 2 * K))
+    c = s.cfg
+    ts = bool(getattr(s, "timestamps", False))
+    dev = logits.device
+    lib = _lib.load()
+    nbytes = int(lib.wt_beam_scores_workspace(B, K))
+    ws = _workspace(dev, ("scores", B, K), nbytes)
+    with torch.cuda.device(dev):
+        st = lib.wt_beam_scores(logits.data_ptr(), s.suppress.data_ptr(), s.begin.data_ptr(), s.t.data_ptr(),
+                                s.cum.data_ptr(), s.hist.data_ptr(), s.max_initial.data_ptr(), _ptr(out),
+                                ns.data_ptr(), top_s.data_ptr(), top_i.data_ptr(), B, K, v, s.hist.shape[1], int(ts),
+                                c.no_speech, (c.no_timestamps or 0) if ts else 0, (c.timestamp_begin or 0) if ts else 0,
+                                c.eot, ws.data_ptr(), nbytes, torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st, what)
+    return top_s, top_i
+
+
+def scores(s, logits: torch.Tensor, out: torch.Tensor, ns: torch.Tensor) -> None:
+    """``out`` [N, V] = log_softmax(masked logits [N, V]) + cum[:, None], ``ns`` [B] the no-speech probabilities --
+    the reference's beam_kernels.scores(s, logits, out, ns) (beam mode), as a drop-in."""
+    best(s, logits, ns, out=out)
+
+
+def step_bookkeeping(s, logits: torch.Tensor, ns: torch.Tensor) -> None:
+    """One step's bookkeeping from the decoder's logits [N, V]: the best 2K candidates of every window, then
+    :func:`update` -- the fused branch of the reference's Search._body (search.py:251-256) without materialising
+    the [N, V] scores."""
+    top_s, top_i = best(s, logits, ns)
+    update(s, top_s, top_i, ns)
