@@ -162,6 +162,58 @@ __device__ __forceinline__ Lse block_lse(Lse x, float *red) {
   return x;
 }
 
+// The logits and suppress / begin flags of one chunk: element u of the chunk is v = 2 * (p0 + (u / 2) * threads +
+// tid) + u % 2 (pairs of consecutive tokens; each thread visits its elements in increasing order). VEC: the row
+// and the flags allow 8-byte / 2-byte pair loads. Past `hi`: x = -inf, flags 0. The begin flags are read only at a
+// window's first step (`first`), where they apply.
+template <bool VEC, bool CHECK = true>
+__device__ __forceinline__ void load_chunk(const float *x, const uint8_t *sup, const uint8_t *beg, int p0, int hi,
+                                           bool first, float (&xv)[kUnroll], bool (&su)[kUnroll],
+                                           bool (&be)[kUnroll]) {
+#pragma unroll
+  for (int j = 0; j < kUnroll / 2; ++j) {
+    const int v = 2 * (p0 + j * kScoreThreads + static_cast<int>(threadIdx.x));
+    if (VEC && (!CHECK || v + 1 < hi)) {
+      const float2 xx = __ldg(reinterpret_cast<const float2 *>(x + v));
+      const unsigned short sp = __ldg(reinterpret_cast<const unsigned short *>(sup + v));
+      const unsigned short bp = first ? __ldg(reinterpret_cast<const unsigned short *>(beg + v)) : 0;
+      xv[2 * j] = xx.x;
+      xv[2 * j + 1] = xx.y;
+      su[2 * j] = (sp & 0xff) != 0;
+      su[2 * j + 1] = (sp >> 8) != 0;
+      be[2 * j] = (bp & 0xff) != 0;
+      be[2 * j + 1] = (bp >> 8) != 0;
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const bool in = v + h < hi;
+        xv[2 * j + h] = in ? __ldg(x + v + h) : -__builtin_huge_valf();
+        su[2 * j + h] = in && __ldg(sup + v + h) != 0;
+        be[2 * j + h] = in && first && __ldg(beg + v + h) != 0;
+      }
+    }
+  }
+}
+// The logits alone of one chunk (pairs when VEC), -inf past hi.
+template <bool VEC>
+__device__ __forceinline__ void load_logits(const float *x, int p0, int hi, float (&xv)[kUnroll]) {
+#pragma unroll
+  for (int j = 0; j < kUnroll / 2; ++j) {
+    const int v = 2 * (p0 + j * kScoreThreads + static_cast<int>(threadIdx.x));
+    if (VEC && v + 1 < hi) {
+      const float2 xx = __ldg(reinterpret_cast<const float2 *>(x + v));
+      xv[2 * j] = xx.x;
+      xv[2 * j + 1] = xx.y;
+    } else {
+      xv[2 * j] = v < hi ? __ldg(x + v) : -__builtin_huge_valf();
+      xv[2 * j + 1] = v + 1 < hi ? __ldg(x + v + 1) : -__builtin_huge_valf();
+    }
+  }
+}
+__device__ __forceinline__ int chunk_v(int p0, int u) {
+  return 2 * (p0 + (u / 2) * kScoreThreads + static_cast<int>(threadIdx.x)) + u % 2;
+}
+
 struct ScoreArgs {
   const float *logits;
   const uint8_t *suppress, *begin;
@@ -188,7 +240,7 @@ struct Exchange {
 
 // One cluster of kScoreCluster CTAs per row, each CTA a contiguous slice of the vocabulary. TS: timestamp rules.
 template <int KK, bool TS>
-__global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreArgs a) {
+__global__ void __launch_bounds__(kScoreThreads, 4) beam_scores_kernel(const ScoreArgs a) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float red[2 * kScoreWarps];
@@ -203,7 +255,7 @@ __global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreA
   const int rank = static_cast<int>(cluster.block_rank());
   const int r = blockIdx.x / kScoreCluster, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = a.K, V = a.V, b = r / K;
-  const int per = (V + kScoreCluster - 1) / kScoreCluster;
+  const int per = ((V + kScoreCluster - 1) / kScoreCluster + 1) & ~1;  // (even: slices start on a pair)
   const int lo = min(V, rank * per), hi = min(V, lo + per);
 
   pdl_wait();
@@ -267,41 +319,76 @@ __global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreA
   float ch_t = -__builtin_huge_valf(), ch_x = ch_t;  // champions: text (all tokens without timestamps), timestamps
   int ch_ti = kNoCand, ch_xi = kNoCand;
   const int tsb = TS ? a.tsb : V;  // (without timestamps every token counts as text)
-  for (int c0 = lo; c0 < hi; c0 += kScoreThreads * kUnroll) {
-    float xv[kUnroll], xm[kUnroll], xt[kUnroll];
-    bool su[kUnroll], be[kUnroll];
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(a.suppress) & 1) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.begin) & 1) == 0;
+  if constexpr (!TS) {
+    // no timestamp rules: the masked maximum is the thread's champion (found per chunk, only when it grows), and
+    // only a window's first row needs the raw sum (its no-speech probability)
+    const bool want_raw = r == b * K;
+    auto chunk = [&](const float (&xv)[kUnroll], const bool (&su)[kUnroll], const bool (&be)[kUnroll], int p0) {
+      float xm[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int v = c0 + u * kScoreThreads + tid;
-      const bool in = v < hi;
-      xv[u] = in ? __ldg(x + v) : -__builtin_huge_valf();
-      su[u] = in && __ldg(a.suppress + v) != 0;
-      be[u] = in && __ldg(a.begin + v) != 0;
-    }
+      for (int u = 0; u < kUnroll; ++u) xm[u] = (su[u] || (first && be[u])) ? kLowest : xv[u];
+      float cm = xm[0];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int v = c0 + u * kScoreThreads + tid;
-      xm[u] = v >= hi ? -__builtin_huge_valf() : (masked(v, su[u], be[u]) ? kLowest : xv[u]);
-      if (TS) {
-        xt[u] = v >= tsb ? xm[u] : -__builtin_huge_valf();
-        if (v < tsb) {
-          mx_text = fmaxf(mx_text, xm[u]);
-          if (xm[u] > ch_t) {
-            ch_t = xm[u];
-            ch_ti = v;
-          }
-        } else if (xm[u] > ch_x) {
-          ch_x = xm[u];
-          ch_xi = v;
-        }
-      } else if (xm[u] > ch_t) {
-        ch_t = xm[u];
-        ch_ti = v;
+      for (int u = 1; u < kUnroll; ++u) cm = fmaxf(cm, xm[u]);
+      if (cm > ch_t) {  // (rare after the first chunks) the first element equal to the chunk's maximum
+        int at = kNoCand;
+#pragma unroll
+        for (int u = kUnroll - 1; u >= 0; --u)
+          if (xm[u] == cm) at = chunk_v(p0, u);
+        ch_t = cm;
+        ch_ti = at;
+      }
+      lse_chunk<kUnroll>(msk, xm);
+      if (want_raw) lse_chunk<kUnroll>(raw, xv);
+    };
+    int p0 = lo / 2;
+    if (vec) {
+      for (; 2 * (p0 + kScoreThreads * (kUnroll / 2)) <= hi; p0 += kScoreThreads * (kUnroll / 2)) {
+        float xv[kUnroll];
+        bool su[kUnroll], be[kUnroll];
+        load_chunk<true, false>(x, a.suppress, a.begin, p0, hi, first, xv, su, be);
+        chunk(xv, su, be, p0);
       }
     }
-    lse_chunk<kUnroll>(raw, xv);
-    lse_chunk<kUnroll>(msk, xm);
-    if (TS) lse_chunk<kUnroll>(tss, xt);
+    for (; 2 * p0 < hi; p0 += kScoreThreads * (kUnroll / 2)) {
+      float xv[kUnroll];
+      bool su[kUnroll], be[kUnroll];
+      load_chunk<false>(x, a.suppress, a.begin, p0, hi, first, xv, su, be);
+      chunk(xv, su, be, p0);
+    }
+  } else {
+    for (int p0 = lo / 2; 2 * p0 < hi; p0 += kScoreThreads * (kUnroll / 2)) {
+      float xv[kUnroll], xm[kUnroll], xt[kUnroll];
+      bool su[kUnroll], be[kUnroll];
+      if (vec) load_chunk<true>(x, a.suppress, a.begin, p0, hi, first, xv, su, be);
+      else load_chunk<false>(x, a.suppress, a.begin, p0, hi, first, xv, su, be);
+  #pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int v = chunk_v(p0, u);
+        xm[u] = v >= hi ? -__builtin_huge_valf() : (masked(v, su[u], be[u]) ? kLowest : xv[u]);
+        if (TS) {
+          xt[u] = v >= tsb ? xm[u] : -__builtin_huge_valf();
+          if (v < tsb) {
+            mx_text = fmaxf(mx_text, xm[u]);
+            if (xm[u] > ch_t) {
+              ch_t = xm[u];
+              ch_ti = v;
+            }
+          } else if (xm[u] > ch_x) {
+            ch_x = xm[u];
+            ch_xi = v;
+          }
+        } else if (xm[u] > ch_t) {
+          ch_t = xm[u];
+          ch_ti = v;
+        }
+      }
+      lse_chunk<kUnroll>(raw, xv);
+      lse_chunk<kUnroll>(msk, xm);
+      if (TS) lse_chunk<kUnroll>(tss, xt);
+    }
   }
   raw = block_lse(raw, red);
   msk = block_lse(msk, red);
@@ -352,9 +439,10 @@ __global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreA
   float ch_s;
   int ch_i;
   if (text_out) {  // the text tokens are now all masked: the thread's first text element stands for them
-    const bool has_text = lo + tid < min(hi, tsb);
+    const int v0 = lo + 2 * tid;  // (the thread's first element)
+    const bool has_text = v0 < min(hi, tsb);
     ch_s = has_text ? kLowest : -__builtin_huge_valf();
-    ch_i = has_text ? lo + tid : kNoCand;
+    ch_i = has_text ? v0 : kNoCand;
   } else {
     ch_s = ch_t;
     ch_i = ch_ti;
@@ -363,18 +451,20 @@ __global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreA
     ch_s = ch_x;
     ch_i = ch_xi;
   }
+  float wm_s = ch_s;
+  int wm_i = ch_i;
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {
-    const float s2 = __shfl_xor_sync(0xffffffffu, ch_s, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, ch_i, o);
-    if (better(s2, i2, ch_s, ch_i)) {
-      ch_s = s2;
-      ch_i = i2;
+    const float s2 = __shfl_xor_sync(0xffffffffu, wm_s, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, wm_i, o);
+    if (better(s2, i2, wm_s, wm_i)) {
+      wm_s = s2;
+      wm_i = i2;
     }
   }
   if (lane == 0) {
-    ex.wm_s[warp] = ch_s;
-    ex.wm_i[warp] = ch_i;
+    ex.wm_s[warp] = wm_s;
+    ex.wm_i[warp] = wm_i;
   }
   cluster.sync();
   __shared__ float thr_sh;
@@ -397,6 +487,67 @@ __global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreA
     }
   }
   __syncthreads();
+  if (thr_sh <= kLowest) {
+    // fewer than kk warps hold an unmasked logit (a window's first step with timestamps, or text masked in favour
+    // of timestamps): the threshold from the threads' champions instead, exact -- the kk-th best of the cluster's
+    float l1s[KK];
+    int l1i[KK];
+#pragma unroll
+    for (int j = 0; j < KK; ++j) {
+      l1s[j] = j == 0 ? ch_s : -__builtin_huge_valf();
+      l1i[j] = j == 0 ? ch_i : kNoCand;
+    }
+    float ws[KK];
+    int wi[KK];
+    warp_select<KK>(l1s, l1i, a.kk, ws, wi);
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < KK; ++j) {
+        wl_s[warp][j] = j < a.kk ? ws[j] : -__builtin_huge_valf();
+        wl_i[warp][j] = j < a.kk ? wi[j] : kNoCand;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < KK; ++j) {
+        l1s[j] = lane < kScoreWarps ? wl_s[lane][j] : -__builtin_huge_valf();
+        l1i[j] = lane < kScoreWarps ? wl_i[lane][j] : kNoCand;
+      }
+      warp_select<KK>(l1s, l1i, a.kk, ws, wi);
+      if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < KK; ++j) {
+          ex.ls[j] = j < a.kk ? ws[j] : -__builtin_huge_valf();
+          ex.li[j] = j < a.kk ? wi[j] : kNoCand;
+        }
+      }
+    }
+    cluster.sync();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < KK; ++j) {
+        const bool have = lane < kScoreCluster;
+        const Exchange<KK> *o = cluster.map_shared_rank(&ex, have ? lane : 0);
+        l1s[j] = have ? o->ls[j] : -__builtin_huge_valf();
+        l1i[j] = have ? o->li[j] : kNoCand;
+      }
+      warp_select<KK>(l1s, l1i, a.kk, ws, wi);
+      if (lane == 0) {
+        float ts = ws[0];
+        int ti = wi[0];
+#pragma unroll
+        for (int j = 1; j < KK; ++j)
+          if (j == a.kk - 1) {
+            ts = ws[j];
+            ti = wi[j];
+          }
+        thr_sh = ts;
+        thr_ish = ti;
+      }
+    }
+    __syncthreads();
+  }
   const float thr = thr_sh;
   const int thr_i = thr_ish;
   // rounding band below the threshold: a few ulps of the score computation's magnitudes
@@ -406,33 +557,48 @@ __global__ void __launch_bounds__(kScoreThreads) beam_scores_kernel(const ScoreA
   // pass 2 (from L2): the scores (written out if asked for) and the candidates, into shared memory
   float *out = a.scores ? a.scores + static_cast<size_t>(r) * V : nullptr;
   const float cut = all_lost ? kLowest : thr_lo;  // (every element below it is no candidate)
-  for (int c0 = lo; c0 < hi; c0 += kScoreThreads * kUnroll) {
-    float xv[kUnroll];
-    bool su[kUnroll], be[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int v = c0 + u * kScoreThreads + tid;
-      const bool in = v < hi;
-      xv[u] = in ? __ldg(x + v) : -__builtin_huge_valf();
-      su[u] = in && __ldg(a.suppress + v) != 0;
-      be[u] = in && __ldg(a.begin + v) != 0;
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int v = c0 + u * kScoreThreads + tid;
-      if (v >= hi) continue;
-      const bool mk = masked(v, su[u], be[u]) || (TS && text_out && v < tsb);
-      const float xm = mk ? kLowest : xv[u];
-      if (out) out[v] = (xm - base - log_sum) + c;
-      if (xm >= cut || all_lost) {
-        const bool cand = all_lost ? v - lo < a.kk : !(xm == thr && v > thr_i);
-        if (cand) {
-          const int slot = atomicAdd(&n_cand, 1);
-          if (slot < a.cap) {
-            cand_s[slot] = (xm - base - log_sum) + c;
-            cand_i[slot] = cand0 + v;
-          }
+  auto consider = [&](int v, float xm) {
+    if (xm >= cut || all_lost) {
+      const bool cand = all_lost ? v - lo < a.kk : !(xm == thr && v > thr_i);
+      if (cand) {
+        const int slot = atomicAdd(&n_cand, 1);
+        if (slot < a.cap) {
+          cand_s[slot] = (xm - base - log_sum) + c;
+          cand_i[slot] = cand0 + v;
         }
+      }
+    }
+  };
+  if (out == nullptr && !all_lost && cut > kLowest) {
+    // the scores are not wanted: the logits alone, and the flags only of the (few) logits above the cut
+    for (int p0 = lo / 2; 2 * p0 < hi; p0 += kScoreThreads * (kUnroll / 2)) {
+      float xv[kUnroll];
+      if (vec) load_logits<true>(x, p0, hi, xv);
+      else load_logits<false>(x, p0, hi, xv);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (xv[u] >= cut) {  // (a masked logit counts as kLowest, below any cut here)
+          const int v = chunk_v(p0, u);
+          const bool mk = masked(v, __ldg(a.suppress + v) != 0, first && __ldg(a.begin + v) != 0) ||
+                          (TS && text_out && v < tsb);
+          consider(v, mk ? kLowest : xv[u]);
+        }
+      }
+    }
+  } else {
+    for (int p0 = lo / 2; 2 * p0 < hi; p0 += kScoreThreads * (kUnroll / 2)) {
+      float xv[kUnroll];
+      bool su[kUnroll], be[kUnroll];
+      if (vec) load_chunk<true>(x, a.suppress, a.begin, p0, hi, first, xv, su, be);
+      else load_chunk<false>(x, a.suppress, a.begin, p0, hi, first, xv, su, be);
+  #pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int v = chunk_v(p0, u);
+        if (v >= hi) continue;
+        const bool mk = masked(v, su[u], be[u]) || (TS && text_out && v < tsb);
+        const float xm = mk ? kLowest : xv[u];
+        if (out) out[v] = (xm - base - log_sum) + c;
+        consider(v, xm);
       }
     }
   }
