@@ -171,6 +171,15 @@ int wt_slot_reset(int32_t *src, const int64_t *slots, int n_slots, int windows, 
                   int prefilled, void *stream);
 
 /* ---------------------------------------------------------------------------------------------------------
+ * The vocabulary projection, fp32 accumulate and output: y [N, V] = x [N, d] . w [V, d]^T (x, w fp16 or bf16,
+ * the same type), on the 5th-generation tensor cores (tcgen05).
+ * Replaces attn_plugin.py:549-560 logits32_triton (kernel :438-455; op body :202-212).
+ *   d a multiple of 8. `err`: a device int (zero it once): non-zero after a bounded wait of the kernel gave up.
+ * ------------------------------------------------------------------------------------------------------- */
+int wt_logits32(int dtype, const void *x, const void *w, float *y, int rows, int vocab, int d_model, int *err,
+                void *stream);
+
+/* ---------------------------------------------------------------------------------------------------------
  * The scoring half of a beam step, feeding wt_beam_update.
  * Replaces beam_kernels.py:351-361 scores() (kernel :36-135 _scores_kernel, beam mode) and the topk of
  * search.py:253 (PyTorch path: search.py:283-289 _choose, :313-338 _timestamp_rules, :369-371, :259-260):

@@ -70,6 +70,12 @@ def test_bad_arguments_return_status_without_a_gpu():
     assert st == _lib.WT_ERR_UNSUPPORTED  # more than 8 beams
     st = lib.wt_beam_scores(*([p] * 11), 2, 5, 51866, 16, 1, 50362, 50363, 0, 50257, p, 1 << 20, None)
     assert st == _lib.WT_ERR_ARG  # timestamps without a timestamp_begin
+    st = lib.wt_logits32(0, p, p, p, 160, 51866, 1280, None, None)
+    assert st == _lib.WT_ERR_ARG  # no error word
+    st = lib.wt_logits32(0, p, p, p, 160, 51866, 1284, p, None)
+    assert st == _lib.WT_ERR_UNSUPPORTED  # d not a multiple of 8
+    st = lib.wt_logits32(2, p, p, p, 160, 51866, 1280, p, None)
+    assert st == _lib.WT_ERR_DTYPE
     st = lib.wt_self_attn(0, p, p, p, p, p, p, 4, 0, 20, 96, 64, None)
     assert st == _lib.WT_ERR_ARG and b"sizes" in lib.wt_last_error()
     st = lib.wt_self_attn(0, p, p, p, p, p, p + 8, 4, 3, 20, 96, 64, None)

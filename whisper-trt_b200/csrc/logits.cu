@@ -1,0 +1,215 @@
+// The vocabulary projection with fp32 accumulation and output: logits [N, V] = x [N, d] . w [V, d]^T, x and w fp16
+// or bf16 -- the reference's logits32 (attn_plugin.py:202-212 op, :438-455 kernel, :549-560 launcher), the one
+// tensor-core-bound piece next to the attention path.
+//
+// B200 design: 5th-generation tensor cores. One CTA per 128-entry vocabulary tile (and 256-row chunk of x): the
+// tile's rows of w are the MMA's A (M = 128), the rows of x its B (N = the rows, padded to 16), the reduction d in
+// 64-element blocks staged by TMA (128-byte swizzle) through a 3-stage ring. Warp 0's lane 0 issues the TMA loads,
+// warp 1's lane 0 the tcgen05.mma instructions (kind::f16, fp32 accumulator in tensor memory); each stage is
+// released by a tcgen05.commit on its "empty" barrier when its MMAs complete, and a final commit signals the
+// accumulator. The 4 warps then read their 32 tensor-memory lanes (vocabulary entries) with tcgen05.ld, 16 rows
+// at a time, and store them as consecutive floats of each output row. Every barrier wait is bounded (a timeout
+// records an error in the device word and the kernel goes on, then frees its tensor memory).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace wt {
+namespace {
+
+constexpr int kLgThreads = 128;
+constexpr int kLgStages = 3;
+constexpr int kLgTileV = 128;   // vocabulary entries per CTA (the MMA's M)
+constexpr int kLgKBlock = 64;   // reduction elements per stage (one 128-byte swizzled row)
+constexpr int kLgMaxRows = 256; // rows of x per CTA (the MMA's N, at most 256)
+constexpr int kLgErrTimeout = 1;
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T, kind::f16 (A and B both fp16 or both bf16), fp32 accumulator
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+// the mbarrier gets one arrival when every tcgen05 operation this thread issued before has completed
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major tile of 128-byte rows with 128-byte swizzle (8-row atoms of 1024 B,
+// the layout a SWIZZLE_128B TMA box of 64 16-bit columns writes): start >> 4, leading offset 16 B (unused for this
+// layout), stride 1024 B between 8-row groups, descriptor version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, A and B of the same 16-bit type, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t idesc_f16(int n, bool bf16) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(kLgTileV >> 4) << 24);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kLgThreads)
+    logits_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                  float *__restrict__ y, int N, int V, int kblocks, int nmma, int tcols, int *err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int a_bytes = kLgTileV * 128, b_bytes = nmma * 128;
+  const int stage_bytes = a_bytes + ((b_bytes + 1023) & ~1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kLgStages * stage_bytes);
+  uint64_t *empty = full + kLgStages;
+  uint64_t *accf = empty + kLgStages;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(accf + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int v0 = blockIdx.x * kLgTileV, n0 = blockIdx.y * kLgMaxRows;
+
+  if (warp == 0) {
+    tmem_alloc(tmem_holder, static_cast<uint32_t>(tcols));
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    prefetch_tensormap(&wmap);
+    prefetch_tensormap(&xmap);
+    for (int s = 0; s < kLgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  pdl_wait();
+  pdl_launch_dependents();
+
+  uint32_t late = 0;  // (producer) stages whose release timed out
+  if (warp == 0 && lane == 0) {
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int s = kb % kLgStages;
+      if (kb >= kLgStages && !mbar_wait_bounded(&empty[s], ((kb / kLgStages) - 1) & 1, err, kLgErrTimeout))
+        late |= 1u << s;
+      unsigned char *st = smem + s * stage_bytes;
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(a_bytes + b_bytes));
+      tma_load_2d(st, &wmap, kb * kLgKBlock, v0, &full[s]);
+      tma_load_2d(st + a_bytes, &xmap, kb * kLgKBlock, n0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    const uint32_t idesc = idesc_f16(nmma, BF16);
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int s = kb % kLgStages;
+      mbar_wait_bounded(&full[s], (kb / kLgStages) & 1, err, kLgErrTimeout);
+      tc_fence_after();
+      const uint32_t a_addr = smem_addr(smem + s * stage_bytes), b_addr = a_addr + a_bytes;
+      const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(b_addr);
+#pragma unroll
+      for (int kk = 0; kk < kLgKBlock / 16; ++kk)  // K = 16 per instruction: +32 bytes along the swizzled row
+        umma_f16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+      umma_commit(&empty[s]);
+    }
+    umma_commit(accf);
+  }
+  __syncwarp();
+  // the accumulator: lane (warp w, thread t) = vocabulary entry v0 + 32 w + t, column n = row n0 + n
+  mbar_wait_bounded(accf, 0, err, kLgErrTimeout);
+  tc_fence_after();
+  const int v = v0 + warp * 32 + lane;
+  for (int c0 = 0; c0 < nmma; c0 += 16) {
+    uint32_t r[16];
+    tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c0), r);
+    tmem_wait_ld();
+    if (v < V) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + c0 + j;
+        if (n < N) y[static_cast<size_t>(n) * V + v] = __uint_as_float(r[j]);
+      }
+    }
+  }
+  // (a timed-out release: wait once more, bounded, for that stage's copies before the shared memory goes away)
+  if (warp == 0 && lane == 0 && late) {
+    for (int kb = kblocks - kLgStages; kb < kblocks; ++kb)
+      if (kb >= 0) mbar_wait_bounded(&full[kb % kLgStages], (kb / kLgStages) & 1, nullptr, 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(tcols));
+}
+
+int g_lg_sm[64] = {};
+
+}  // namespace
+}  // namespace wt
+
+extern "C" int wt_logits32(int dtype, const void *x, const void *w, float *y, int rows, int vocab, int d_model,
+                           int *err, void *stream) {
+  using namespace wt;
+  WT_REQUIRE(rows > 0 && vocab > 0 && d_model > 0, WT_ERR_ARG,
+             "logits32: sizes must be positive (rows %d, vocab %d, d_model %d)", rows, vocab, d_model);
+  WT_REQUIRE(x && w && y && err, WT_ERR_ARG, "logits32: null pointer");
+  WT_ALIGNED(x);
+  WT_ALIGNED(w);
+  WT_ALIGNED(y);
+  WT_REQUIRE(d_model % 8 == 0, WT_ERR_UNSUPPORTED, "logits32: d_model %d is not a multiple of 8", d_model);
+  WT_REQUIRE(dtype == WT_F16 || dtype == WT_BF16, WT_ERR_DTYPE, "logits32: unknown dtype %d", dtype);
+  const int chunks = (rows + kLgMaxRows - 1) / kLgMaxRows;
+  const int nrows = rows < kLgMaxRows ? rows : kLgMaxRows;
+  const int nmma = (nrows + 15) / 16 * 16;
+  int tcols = 32;
+  while (tcols < nmma) tcols <<= 1;
+  CUtensorMap wm, xm;
+  int st = encode_tile_map(&wm, w, static_cast<unsigned long long>(vocab), static_cast<unsigned long long>(d_model),
+                           kLgTileV, dtype);
+  if (st != WT_OK) return st;
+  st = encode_tile_map(&xm, x, static_cast<unsigned long long>(rows), static_cast<unsigned long long>(d_model), nmma,
+                       dtype);
+  if (st != WT_OK) return st;
+  const int stage_bytes = kLgTileV * 128 + (nmma * 128 + 1023) / 1024 * 1024;
+  const int smem = 1024 + kLgStages * stage_bytes + (2 * kLgStages + 1) * 8 + 16;
+  const int kblocks = (d_model + kLgKBlock - 1) / kLgKBlock;
+  auto kernel = dtype == WT_BF16 ? logits_kernel<true> : logits_kernel<false>;
+  static int attr_bytes[2] = {0, 0};
+  if (smem > attr_bytes[dtype]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_bytes[dtype] = smem;
+  }
+  (void)g_lg_sm;
+  return launch("logits32", kernel, dim3((vocab + kLgTileV - 1) / kLgTileV, chunks), dim3(kLgThreads), smem, stream,
+                wm, xm, y, rows, vocab, kblocks, nmma, tcols, err);
+}

@@ -10,7 +10,8 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 }  // namespace
 
-int encode_rows128_map(CUtensorMap *map, const void *base, unsigned long long rows, int box_rows, int dtype) {
+int encode_tile_map(CUtensorMap *map, const void *base, unsigned long long rows, unsigned long long cols,
+                    int box_rows, int dtype) {
   std::call_once(g_encode_once, [] {
     void *fn = nullptr;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
@@ -20,8 +21,8 @@ int encode_rows128_map(CUtensorMap *map, const void *base, unsigned long long ro
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
   if (g_encode == nullptr) return fail(WT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {128};
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
   const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t elem[2] = {1, 1};
   const CUresult r =
@@ -30,6 +31,10 @@ int encode_rows128_map(CUtensorMap *map, const void *base, unsigned long long ro
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(WT_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
   return WT_OK;
+}
+
+int encode_rows128_map(CUtensorMap *map, const void *base, unsigned long long rows, int box_rows, int dtype) {
+  return encode_tile_map(map, base, rows, 64, box_rows, dtype);
 }
 
 }  // namespace wt

@@ -13,6 +13,10 @@ namespace wt {
 // Encode a 2D tiled tensor map over a row-major [rows, 64] tensor of 16-bit elements (128-byte rows) with boxes of
 // `box_rows` rows, 128-byte swizzle (16-byte chunk c of row r lands at chunk c ^ (r % 8)), zero fill out of bounds.
 int encode_rows128_map(CUtensorMap *map, const void *base, unsigned long long rows, int box_rows, int dtype);
+// The same for a row-major [rows, cols] tensor of 16-bit elements (cols a multiple of 8: 16-byte row stride), boxes of
+// 64 columns x `box_rows` rows; elements outside the tensor read as zero.
+int encode_tile_map(CUtensorMap *map, const void *base, unsigned long long rows, unsigned long long cols,
+                    int box_rows, int dtype);
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -41,6 +41,7 @@ SIGNATURES = {
                                 c_int, c_int, c_void]),
     "wt_beam_update": (c_int, [c_void] * 18 + [c_int] * 8 + [c_void]),
     "wt_slot_reset": (c_int, [c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void]),
+    "wt_logits32": (c_int, [c_int, c_void, c_void, c_void, c_int, c_int, c_int, c_void, c_void]),
     "wt_beam_scores_workspace": (c_size, [c_int, c_int]),
     "wt_beam_scores": (c_int, [c_void] * 11 + [c_int] * 9 + [c_void, c_size, c_void]),
 }

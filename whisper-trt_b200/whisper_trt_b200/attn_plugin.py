@@ -83,7 +83,7 @@ def workspace_errors() -> int:
     Reads device memory: synchronises."""
     err = 0
     for (dev, kind, shape), ws in _workspaces.items():
-        if kind == "cross":
+        if kind in ("cross", "logits"):
             err |= int(ws[:4].view(torch.int32).item())
     return err
 
@@ -287,7 +287,46 @@ def cross_attn_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, config=
     return y
 
 
+# --- vocabulary projection -----------------------------------------------------------------------------------
+def logits32_triton(x: torch.Tensor, w: torch.Tensor, config=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [B, S, d] (fp16 / bf16) @ w [V, d]^T accumulated and returned in fp32 -> [B, S, V] (into ``out`` if given),
+    on the tcgen05 tensor cores. Reference: attn_plugin.py:549-560 (kernel :438-455, op :202-212). ``config`` is
+    accepted for call-compatibility and ignored."""
+    what = "logits32"
+    if x.dim() != 3 or w.dim() != 2 or x.shape[2] != w.shape[1]:
+        raise ValueError(f"{what}: x must be [B, S, d] and w [V, d] (got {tuple(x.shape)}, {tuple(w.shape)})")
+    b, s, d = x.shape
+    v = w.shape[0]
+    code = _dtype_code(x, what)
+    if w.dtype != x.dtype:
+        raise TypeError(f"{what}: x and w must have the same dtype")
+    x = x.contiguous()
+    dev = _cuda(what, x, w)
+    y = torch.empty(b, s, v, dtype=torch.float32, device=dev) if out is None else out
+    if y.shape != (b, s, v) or y.dtype != torch.float32 or not y.is_contiguous():
+        raise ValueError(f"{what}: out must be a contiguous [B, S, V] float32 tensor")
+    if b * s == 0:
+        return y
+    err = _workspace(dev, "logits", (), 256)
+    with torch.cuda.device(dev):
+        st = _lib.load().wt_logits32(code, x.data_ptr(), w.data_ptr(), y.data_ptr(), b * s, v, d, err.data_ptr(),
+                                     _stream(dev))
+    _lib.check(st, what)
+    return y
+
+
 # --- torch custom ops (graph-capturable, with fake kernels for tracing) ------------------------------------
+@torch.library.custom_op(f"{NAMESPACE}::logits32", mutates_args=())
+def logits32(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x [B, S, d] @ w [V, d]^T in fp32 (reference op ``whisper_trt::logits32``, attn_plugin.py:202-212)."""
+    return logits32_triton(x, w)
+
+
+@logits32.register_fake
+def _(x, w):
+    return x.new_empty(x.shape[0], x.shape[1], w.shape[0], dtype=torch.float32)
+
+
 @torch.library.custom_op(f"{NAMESPACE}::self_attn", mutates_args=())
 def self_attn(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: torch.Tensor,
               src: torch.Tensor) -> torch.Tensor:
@@ -361,5 +400,5 @@ def install(module) -> None:
     """Route a reference ``whisper_trt.attn_plugin`` module's launchers to these kernels (in place), so its callers
     -- ``TritonDecoderBackend.step_fn`` (runtime.py:134-151) among them -- run on them unchanged."""
     for name in ("self_attn_triton", "self_attn_step_triton", "cross_attn_split_triton",
-                 "cross_attn_combine_triton", "cross_attn_triton", "self_attn_step_config"):
+                 "cross_attn_combine_triton", "cross_attn_triton", "self_attn_step_config", "logits32_triton"):
         setattr(module, name, globals()[name])
