@@ -1,0 +1,167 @@
+"""Time one kernel of the package on synthetic inputs (CUDA events on the launching stream, warm) and print one
+JSON line -- the per-kernel numbers beside bench.py's whole-step line, and the commands the ncu summaries use.
+
+    python -m whisper_trt_b200.kernel_bench beam_scores --windows 32 --beams 5 [--timestamps] [--reps 20]
+    python -m whisper_trt_b200.kernel_bench logits32 --rows 160
+    python -m whisper_trt_b200.kernel_bench prompt --rows 80 --tokens 224 --cached 0
+    python -m whisper_trt_b200.kernel_bench cross --windows 32 --beams 5
+    python -m whisper_trt_b200.kernel_bench self_step --rows 160 --cache-lo 4 --cache-hi 224
+
+(from the ``whisper-trt_b200`` directory, or with it on PYTHONPATH). Inputs are seeded N(0, 1) (weights N(0, 0.02));
+several layers' worth of inputs rotate so that consecutive calls do not hit L2 for the bytes they stream.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from types import SimpleNamespace
+
+import torch
+
+from . import attn_plugin as ap
+from . import slots
+
+
+def _time(fn, reps: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps * 1e-3
+
+
+def beam_scores(a) -> dict:
+    dev, V, W, K = "cuda", a.vocab, a.windows, a.beams
+    g = torch.Generator(device=dev).manual_seed(0)
+    cfg = SimpleNamespace(no_speech=50362, no_timestamps=50363, timestamp_begin=50365, eot=50257, vocab_size=V)
+    s = SimpleNamespace(K=K, cfg=cfg, timestamps=a.timestamps, suppress=torch.zeros(V, dtype=torch.bool, device=dev),
+                        begin=torch.zeros(V, dtype=torch.bool, device=dev),
+                        t=torch.full((W,), 5, dtype=torch.int64, device=dev),
+                        cum=torch.zeros(W * K, device=dev), hist=torch.zeros(W * K, 224, dtype=torch.int64, device=dev),
+                        max_initial=torch.tensor([50], device=dev))
+    logits = torch.randn(W * K, V, generator=g, device=dev)
+    ns = torch.empty(W, device=dev)
+    sec = _time(lambda: slots.best(s, logits, ns), a.reps)
+    nb = logits.numel() * 4
+    return {"kernel": "beam_scores", "windows": W, "beams": K, "vocab": V, "timestamps": a.timestamps,
+            "us": round(sec * 1e6, 2), "gbs": round(nb / sec / 1e9, 1)}
+
+
+def logits32(a) -> dict:
+    dev, V, d, n = "cuda", a.vocab, a.d_model, a.rows
+    g = torch.Generator(device=dev).manual_seed(0)
+    L = 3
+    x = torch.randn(L, n, 1, d, generator=g, device=dev).half()
+    w = (torch.randn(L, V, d, generator=g, device=dev) * 0.02).half()
+    out = torch.empty(n, 1, V, device=dev)
+    i = [0]
+
+    def run():
+        j = i[0] % L
+        i[0] += 1
+        ap.logits32_triton(x[j], w[j], out=out)
+
+    sec = _time(run, a.reps)
+    nb = V * d * 2 + n * d * 2 + n * V * 4
+    return {"kernel": "logits32", "rows": n, "vocab": V, "d_model": d, "us": round(sec * 1e6, 2),
+            "gbs": round(nb / sec / 1e9, 1), "tflops": round(2 * n * V * d / sec / 1e12, 1)}
+
+
+def prompt(a) -> dict:
+    dev, N, S, C, H = "cuda", a.rows, a.tokens, a.capacity, 20
+    g = torch.Generator(device=dev).manual_seed(0)
+    L = 4
+    qkv = torch.randn(L, N, S, 3 * H * 64, generator=g, device=dev).half()
+    kc = torch.randn(N, H, C, 64, generator=g, device=dev).half()
+    vc = torch.randn(N, H, C, 64, generator=g, device=dev).half()
+    off = torch.full((N,), a.cached, dtype=torch.long, device=dev)
+    src = torch.arange(N, dtype=torch.int32, device=dev)[:, None].expand(N, C).contiguous()
+    y = torch.empty(N, S, H * 64, device=dev, dtype=torch.float16)
+    i = [0]
+
+    def run():
+        j = i[0] % L
+        i[0] += 1
+        ap.self_attn_triton(qkv[j], kc, vc, off, src, out=y)
+
+    sec = _time(run, a.reps)
+    flops = N * H * 64 * 4 * (S * a.cached + S * (S + 1) / 2)
+    return {"kernel": "self_attn (prompt)", "rows": N, "tokens": S, "cached": a.cached, "us": round(sec * 1e6, 2),
+            "tflops": round(flops / sec / 1e12, 1)}
+
+
+def cross(a) -> dict:
+    dev, W, K, H, T = "cuda", a.windows, a.beams, 20, 1500
+    g = torch.Generator(device=dev).manual_seed(0)
+    L = max(2, -(-400_000_000 // (W * H * T * 64 * 4)))
+    k = torch.randn(L, W, H, T, 64, generator=g, device=dev).half()
+    v = torch.randn(L, W, H, T, 64, generator=g, device=dev).half()
+    q = torch.randn(L, W, K, H * 64, generator=g, device=dev).half()
+    out = torch.empty(W, K, H * 64, device=dev, dtype=torch.float16)
+    i = [0]
+
+    def run():
+        j = i[0] % L
+        i[0] += 1
+        ap.cross_attn_triton(q[j], k[j], v[j], out=out)
+
+    sec = _time(run, a.reps)
+    nb = W * H * T * 64 * 4 + W * K * H * 64 * 4
+    return {"kernel": "cross_attn", "windows": W, "queries": K, "us": round(sec * 1e6, 2),
+            "gbs": round(nb / sec / 1e9, 1)}
+
+
+def self_step(a) -> dict:
+    dev, N, C, H = "cuda", a.rows, a.capacity, 20
+    g = torch.Generator(device=dev).manual_seed(0)
+    L = 8
+    kc = torch.randn(L, N, H, C, 64, generator=g, device=dev).half()
+    vc = torch.randn(L, N, H, C, 64, generator=g, device=dev).half()
+    qkv = torch.randn(L, N, 1, 3 * H * 64, generator=g, device=dev).half()
+    off = torch.randint(a.cache_lo, a.cache_hi + 1, (N // 5,), generator=g, device=dev).repeat_interleave(5)
+    src = ((torch.arange(N, device=dev) // 5 * 5)[:, None]
+           + torch.randint(0, 5, (N, C), generator=g, device=dev)).to(torch.int32)
+    y = torch.empty(N, 1, H * 64, device=dev, dtype=torch.float16)
+    i = [0]
+
+    def run():
+        j = i[0] % L
+        i[0] += 1
+        ap.self_attn_step_triton(qkv[j], kc[j], vc[j], off, src, out=y)
+
+    sec = _time(run, a.reps)
+    nb = int(off.sum()) * H * 64 * 4 + N * 3 * H * 64 * 2
+    return {"kernel": "self_attn_step", "rows": N, "capacity": C, "us": round(sec * 1e6, 2),
+            "gbs": round(nb / sec / 1e9, 1)}
+
+
+def main() -> None:
+    p = argparse.ArgumentParser()
+    p.add_argument("kernel", choices=["beam_scores", "logits32", "prompt", "cross", "self_step"])
+    p.add_argument("--windows", type=int, default=32)
+    p.add_argument("--beams", type=int, default=5)
+    p.add_argument("--vocab", type=int, default=51866)
+    p.add_argument("--timestamps", action="store_true")
+    p.add_argument("--rows", type=int, default=160)
+    p.add_argument("--d-model", type=int, default=1280)
+    p.add_argument("--tokens", type=int, default=224)
+    p.add_argument("--cached", type=int, default=0)
+    p.add_argument("--capacity", type=int, default=448)
+    p.add_argument("--cache-lo", type=int, default=4)
+    p.add_argument("--cache-hi", type=int, default=224)
+    p.add_argument("--reps", type=int, default=20)
+    a = p.parse_args()
+    assert torch.cuda.is_available(), "needs a CUDA GPU"
+    if a.kernel == "self_step" and a.capacity == 448:
+        a.capacity = 228
+    print(json.dumps(globals()[a.kernel](a)))
+
+
+if __name__ == "__main__":
+    main()
