@@ -131,16 +131,16 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   const int cap = (C + splits - 1) / splits;
   const int lo = sp * cap;
   const int lim = min(C, lo + cap) - lo;
+  // (the whole slice, not only the slots below the offset: its loads then go out together with the offset's)
   const int64_t off64 = offset[r];
-  const int off = static_cast<int>(off64 < 0 ? 0 : (off64 > C ? C : off64));
-  const int hi = max(lo, min(off, lo + cap));  // keys [lo, hi) of this split
   const int32_t *srow = src + static_cast<size_t>(r) * C + lo;
-  for (int i = threadIdx.x; i < hi - lo; i += kWarpsPerCta * 32) {
+  for (int i = threadIdx.x; i < lim; i += kWarpsPerCta * 32) {
     const int v = srow[i];
     rows_s[i] = v < 0 ? 0 : (v > N - 1 ? N - 1 : v);
   }
+  const int off = static_cast<int>(off64 < 0 ? 0 : (off64 > C ? C : off64));
+  const int hi = max(lo, min(off, lo + cap));  // keys [lo, hi) of this split
   __syncthreads();
-  (void)lim;
 
   // this warp's quarter: whole stages [st0, st1) of the split's range
   const int nst_all = (hi - lo + KPS - 1) / KPS;

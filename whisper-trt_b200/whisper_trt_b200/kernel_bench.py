@@ -24,10 +24,13 @@ from . import slots
 
 
 def _time(fn, reps: int) -> float:
+    """Device time per call: the calls are queued behind a spin of the GPU so that the host's launch overhead does
+    not space them out."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(100_000_000)
     e0.record()
     for _ in range(reps):
         fn()
