@@ -5,12 +5,14 @@
 //
 // One CTA per (row, head, block of 64 queries), 4 warps of 16 queries each. Queries are the M of
 // mma.sync.m16n8k16 (f32 accumulate), keys the N, the head dim the reduction; P stays in registers between
-// S = Q K^T and O += P V (the S accumulator layout is the A operand layout of the next mma), split into a hi and a
-// lo half-precision part so the product keeps ~fp32 accuracy. Key blocks of 64 keys are staged by cp.async into
-// 128-byte-swizzled shared tiles (double-buffered): first the row's cache slots, each key row from the row the slot
+// S = Q K^T and O += P V (the S accumulator layout is the A operand layout of the next mma; P rounded to the input
+// type as the reference's kernel rounds it, and for bf16 split into hi + lo parts to stay near fp32 accuracy). Key
+// blocks of 64 keys are staged by cp.async into 128-byte-swizzled shared tiles (double-buffered): first the row's cache slots, each key row from the row the slot
 // table names (the table's slice staged in shared memory first, so no key load waits on an index load), then the
 // new tokens' keys/values straight from qkv. Out-of-range keys are zero-filled and masked; offset is clamped to
 // [0, C] and slot-table rows to [0, N-1], as the reference's kernels do.
+#include <type_traits>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -189,33 +191,39 @@ __global__ void __launch_bounds__(kPThreads)
         o[i][2] *= a1;
         o[i][3] *= a1;
       }
-      // O += P V over 16 keys at a time; P = hi + lo, both in T
+      // O += P V over 16 keys at a time; P in T as the reference's kernel does (attn_plugin.py:272); bf16, whose
+      // 8-bit significand would cost more than the 2e-3 bar, as hi + lo
+      constexpr bool kSplit = !std::is_same<T, __half>::value;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         if (2 * kk < nact) {
-          uint32_t ph[4], pl[4];
+          uint32_t ph[4], pl[4] = {0u, 0u, 0u, 0u};
           const float *pa = sacc[2 * kk], *pb = sacc[2 * kk + 1];
           ph[0] = E::from_float2(pa[0], pa[1]);
           ph[1] = E::from_float2(pa[2], pa[3]);
           ph[2] = E::from_float2(pb[0], pb[1]);
           ph[3] = E::from_float2(pb[2], pb[3]);
-          float2 f;
-          f = E::to_float2(ph[0]);
-          pl[0] = E::from_float2(pa[0] - f.x, pa[1] - f.y);
-          f = E::to_float2(ph[1]);
-          pl[1] = E::from_float2(pa[2] - f.x, pa[3] - f.y);
-          f = E::to_float2(ph[2]);
-          pl[2] = E::from_float2(pb[0] - f.x, pb[1] - f.y);
-          f = E::to_float2(ph[3]);
-          pl[3] = E::from_float2(pb[2] - f.x, pb[3] - f.y);
+          if (kSplit) {
+            float2 f;
+            f = E::to_float2(ph[0]);
+            pl[0] = E::from_float2(pa[0] - f.x, pa[1] - f.y);
+            f = E::to_float2(ph[1]);
+            pl[1] = E::from_float2(pa[2] - f.x, pa[3] - f.y);
+            f = E::to_float2(ph[2]);
+            pl[2] = E::from_float2(pb[0] - f.x, pb[1] - f.y);
+            f = E::to_float2(ph[3]);
+            pl[3] = E::from_float2(pb[2] - f.x, pb[3] - f.y);
+          }
 #pragma unroll
           for (int dp = 0; dp < 4; ++dp) {
             uint32_t vf[4];
             ldmatrix_x4_trans(vf, vd + swizzle128(16 * kk + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * dp + (lane >> 4)));
             Mma<T>::run(o[2 * dp], ph[0], ph[1], ph[2], ph[3], vf[0], vf[1]);
-            Mma<T>::run(o[2 * dp], pl[0], pl[1], pl[2], pl[3], vf[0], vf[1]);
             Mma<T>::run(o[2 * dp + 1], ph[0], ph[1], ph[2], ph[3], vf[2], vf[3]);
-            Mma<T>::run(o[2 * dp + 1], pl[0], pl[1], pl[2], pl[3], vf[2], vf[3]);
+            if (kSplit) {
+              Mma<T>::run(o[2 * dp], pl[0], pl[1], pl[2], pl[3], vf[0], vf[1]);
+              Mma<T>::run(o[2 * dp + 1], pl[0], pl[1], pl[2], pl[3], vf[2], vf[3]);
+            }
           }
         }
       }
