@@ -248,15 +248,6 @@ int fused_splits(int W, int S, int H, int Tn) {
   return static_cast<int>(p);
 }
 
-size_t fused_workspace(int W, int S, int H, int Tn) {
-  const int nt = query_tiles(S);
-  const int qgs = (S + nt * 8 - 1) / (nt * 8);
-  const long long units = static_cast<long long>(W) * H * qgs;
-  const int P = fused_splits(W, S, H, Tn);
-  const size_t counters = (static_cast<size_t>(units) * sizeof(int) + 255) / 256 * 256;
-  return counters + static_cast<size_t>(units) * P * nt * 8 * (kD + 2) * sizeof(float);
-}
-
 float qk_scale() { return static_cast<float>(1.0 / sqrt(static_cast<double>(kD)) * 1.4426950408889634); }
 
 template <typename T, bool FUSED>

@@ -81,11 +81,6 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Prefetch `bytes` (a multiple of 16) at a 16-byte aligned global address into L2.
-__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 template <int LPK>
 __device__ __forceinline__ float group_sum(float x) {
 #pragma unroll
@@ -368,13 +363,11 @@ int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *off
 
 extern "C" {
 
-static constexpr int kMaxSplitKeysPublic = wt::kMaxSplitKeys;
-
 int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim) {
   // one CTA of 4 warps per (row, head, split), at most 1024 slots each; split further only when the (row, head)
   // pairs alone would leave the SMs short of CTAs (< 2 per SM): splitting costs a partial and a combine
   const long long items = static_cast<long long>(rows) * heads;
-  long long s = (capacity + kMaxSplitKeysPublic - 1) / kMaxSplitKeysPublic;
+  long long s = (capacity + wt::kMaxSplitKeys - 1) / wt::kMaxSplitKeys;
   const long long want = (148LL * 2 + items - 1) / items;
   if (want > s) s = want;
   const long long cap = (capacity + 63) / 64;  // at least ~64 keys (16 per warp) per split
