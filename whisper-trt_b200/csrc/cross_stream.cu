@@ -4,16 +4,22 @@
 // (window, head) over the window's T encoder frames, scores in log2 units; fp32 accumulation.
 //
 // B200 design. The work is the flat sequence of (window, head, query group, 16-key block) units -- 94 blocks per
-// (window, head) at T = 1500 -- cut into one equal contiguous range per warp of a grid of one CTA per SM
+// (window, head) at T = 1500 -- cut into one equal contiguous range per streaming warp of a persistent grid
 // ("stream-K": every warp streams the same number of bytes, no wave tail whatever the window count):
-//   * each warp owns a ring of 4 stages in shared memory; its lane 0 issues 2D TMA loads (16 rows x 128 bytes of K and
-//     of V, 128-byte swizzle) that complete on the stage's mbarrier, keeping three blocks in flight while the warp
-//     computes the fourth -- no registers are held by loads in flight;
+//   * each streaming warp owns a ring of stages in shared memory; its lane 0 issues 2D TMA loads (16 rows x 128 bytes
+//     of K and of V, 128-byte swizzle) that complete on the stage's mbarrier, keeping the other stages in flight
+//     while the warp computes -- no registers are held by loads in flight;
 //   * the block's mma operands are read from the swizzled tile with bank-conflict-free 16-byte shared loads and
 //     go through the same tensor-core math as the split kernel (cross_math.cuh);
-//   * when a warp's range crosses into the next (window, head), it writes its partial (acc, m, l) for the finished
-//     one; the warp that completes a (window, head) -- an atomic count of its blocks, no waiting -- combines the
-//     partials (at most ceil(94 / blocks per warp) + 1 of them) and writes the output.
+//   * a unit wholly inside one warp's range goes straight to the output; the range's first and last units are shared
+//     with the neighbouring warps: the warp stores its partial (acc, m, l) for them, their counters count the blocks
+//     done, and the warp that completes a unit -- no waiting -- combines its partials (at most
+//     ceil(94 / blocks per warp) + 1) into the output;
+//   * a streaming warp never executes a GPU-scope fence while its loads are in flight: such a fence (which a count
+//     needs after the partial's stores) stalled the warp for about as long as eight blocks take to stream. The first
+//     unit's count, due in mid-range, is left to the CTA's one service warp, which issues no loads: the streaming
+//     warp stores its partial and arrives on an mbarrier (a CTA-scope release), and the service warp fences and
+//     counts. The last unit is counted by its warp at the end of its range, when nothing of its own is in flight.
 // Every mbarrier wait is bounded: a wait that times out records an error code in the workspace and the warp goes on.
 // With programmatic dependent launch the first TMA loads are issued before the preceding kernel has finished (the
 // cross keys/values are not its output); the queries are read after it, one unit ahead of their use.
@@ -30,17 +36,20 @@ constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
 constexpr int kErrTimeout = 1;
 constexpr int kPart = kD + 4;  // floats per query of a partial: acc[64], m, l, 2 pad (16-byte aligned records)
 
-// Launch shapes: warps per CTA x ring stages per warp x CTAs per SM. Shared memory: warps * stages * 4 KB per CTA.
-// Default: 6 warps x 4 stages, 2 CTAs per SM (measured best at 8 and 32 windows; 4x6, 3x8, 5x5 x 2 CTAs and
-// 12x4 x 1 CTA were slower).
+// Launch shapes: streaming warps per CTA (plus the service warp) x ring stages per warp x CTAs per SM. Shared
+// memory: warps * stages * 4 KB per CTA. Default: 5 (+1) warps x 5 stages, 2 CTAs per SM: 10 streaming warps and
+// 200 KB of ring per SM (before the service warp: 6 warps x 4 stages x 2 CTAs measured best at 8 and 32 windows;
+// 4x6, 3x8, 5x5 x 2 CTAs and 12x4 x 1 CTA were slower).
 struct Shape {
   int warps, stages;
   bool pair;  // two 16-key blocks per step of the online softmax
   int ctas;   // CTAs per SM
 };
-constexpr Shape kShapes[] = {{12, 4, false, 1}, {12, 4, true, 1}, {6, 4, true, 2}, {8, 4, true, 1}, {4, 4, true, 3}};
+constexpr Shape kShapes[] = {{11, 4, false, 1}, {11, 4, true, 1}, {5, 5, true, 2}, {5, 4, true, 2}, {11, 5, true, 1}};
 
-constexpr int smem_bytes(int warps, int stages) { return warps * stages * kStageBytes + warps * stages * 8 + 1024; }
+constexpr int smem_bytes(int warps, int stages) {
+  return warps * stages * kStageBytes + warps * stages * 8 + warps * 24 + 1024;
+}
 
 struct StreamArgs {
   const void *q;
@@ -75,13 +84,11 @@ __device__ __forceinline__ void reset_state(State<NT> &st) {
   }
 }
 
-// The warp's partial for unit u (its `nblk` blocks of it) -> workspace, then its block count added to the unit's
-// counter with release semantics (one lane, after a warp barrier: no fence stalls the streaming warp). Returns, in
-// lane 0, whether this warp completed the unit -- the caller looks at it only when its range is done, so the
-// atomic's round trip never stalls the stream.
+// The warp's partial for unit u -> workspace (plain stores: nothing waits for them here; the count that publishes
+// them comes later, behind a fence -- see publish() and serve_requests()).
 template <int NT>
-__device__ __forceinline__ int write_partial(State<NT> &st, const StreamArgs &a, long long u, int nblk, long long gw,
-                                             int lane) {
+__device__ __forceinline__ void store_partial(State<NT> &st, const StreamArgs &a, long long u, long long gw,
+                                              int lane) {
   const int g = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -107,14 +114,47 @@ __device__ __forceinline__ int write_partial(State<NT> &st, const StreamArgs &a,
         rq[kD + 1] = st.l[nt][j];
       }
     }
+}
+
+// The warp's block count for unit u added to the unit's counter, after a warp barrier and a release fence that order
+// the partial this warp stored before it. Returns, in lane 0, whether this warp completed the unit.
+__device__ __forceinline__ bool publish(const StreamArgs &a, long long u, int nblk, int lane) {
   __syncwarp();
   int old = 0;
-  if (lane == 0)
-    asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;"
-                 : "=r"(old)
-                 : "l"(a.counters + u), "r"(nblk)
-                 : "memory");
+  if (lane == 0) {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a.counters + u), "r"(nblk) : "memory");
+  }
   return old + nblk == a.bpu;
+}
+
+// A unit this warp attended whole: its output straight from the registers (acc / l per query; the running maximum is
+// common to both), no partial and no counter.
+template <typename T, int NT>
+__device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a, long long u, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+  const int wh = static_cast<int>(u / a.QG), qg = static_cast<int>(u % a.QG);
+  const int w = wh / a.H, h = wh - w * a.H;
+  const size_t HD = static_cast<size_t>(a.H) * kD;
+  T *y = static_cast<T *>(a.y);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float l = st.l[nt][j];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      const int qi = qg * NT * 8 + nt * 8 + 2 * c + j;
+      if (qi < a.S) {
+        const float inv = 1.f / l;
+        T *yr = y + (static_cast<size_t>(w) * a.S + qi) * HD + static_cast<size_t>(h) * kD;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          yr[16 * i + g] = Elem<T>::from_float(st.o[nt][i][j] * inv);
+          yr[16 * i + g + 8] = Elem<T>::from_float(st.o[nt][i][j + 2] * inv);
+        }
+      }
+    }
 }
 
 // The warp that completed unit u: every partial of u -> the output (then the counter back to zero). Each lane owns
@@ -124,6 +164,7 @@ __device__ __forceinline__ int write_partial(State<NT> &st, const StreamArgs &a,
 constexpr int kCombineSlots = 4;
 template <typename T, int NT>
 __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
+  __syncwarp();
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
   const long long fw = first_warp(u, a.bpu, a.per_warp);
   const int nslots = static_cast<int>(last_warp(u, a.bpu, a.per_warp) - fw + 1);
@@ -209,8 +250,38 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
   if (lane == 0) a.counters[u] = 0;  // left zeroed for the next launch
 }
 
-template <typename T, int NT, int kStreamWarps, int kStreamStages, bool kPair>
-__global__ void __launch_bounds__(kStreamWarps * 32)
+// The CTA's service warp: lane i waits for streaming warp i's request (its first unit's partial stored, or none),
+// then adds the warp's block count to the unit's counter behind a GPU-scope fence -- the fence covers the streaming
+// warp's stores, ordered before its mbarrier arrival, which this lane's wait acquires. Units it completes it
+// combines itself. The polls are bounded: on a timeout the error word gets a code and the warp returns.
+template <typename T, int NT, int kStreamWarps>
+__device__ void serve_requests(const StreamArgs &a, uint64_t *req_bar, const long long *req_u, const int *req_n,
+                               int lane) {
+  bool waiting = lane < kStreamWarps;
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    long long u = -1;
+    bool completed = false;
+    if (waiting && mbar_try_wait(&req_bar[lane], 0)) {
+      waiting = false;
+      u = req_u[lane];
+      if (u >= 0) {
+        const int nb = req_n[lane];
+        int old = 0;
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a.counters + u), "r"(nb) : "memory");
+        completed = old + nb == a.bpu;
+      }
+    }
+    for (unsigned m = __ballot_sync(0xffffffffu, completed); m; m &= m - 1)
+      combine_unit<T, NT>(a, __shfl_sync(0xffffffffu, u, __ffs(m) - 1), lane);
+    if (!__any_sync(0xffffffffu, waiting)) return;
+    if (it > 64) __nanosleep(64);
+  }
+  if (lane == 0) atomicExch(a.err, kErrTimeout);
+}
+
+template <typename T, int NT, int kStreamWarps, int kStreamStages, bool kPair, int kCtas>
+__global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
     cross_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                         const StreamArgs a) {
   constexpr int kWarpRing = kStreamStages * kStageBytes;
@@ -219,6 +290,18 @@ __global__ void __launch_bounds__(kStreamWarps * 32)
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
+  uint64_t *req_bar = reinterpret_cast<uint64_t *>(smem + kStreamWarps * kWarpRing) + kStreamWarps * kStreamStages;
+  long long *req_u = reinterpret_cast<long long *>(req_bar + kStreamWarps);
+  int *req_n = reinterpret_cast<int *>(req_u + kStreamWarps);
+  if (warp == kStreamWarps) {  // the service warp
+    if (lane < kStreamWarps) mbar_init(&req_bar[lane], 1);
+    fence_mbar_init();
+    __syncthreads();
+    pdl_wait();
+    pdl_launch_dependents();
+    serve_requests<T, NT, kStreamWarps>(a, req_bar, req_u, req_n, lane);
+    return;
+  }
   unsigned char *ring = smem + warp * kWarpRing;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStreamWarps * kWarpRing) + warp * kStreamStages;
   const long long gw = static_cast<long long>(blockIdx.x) * kStreamWarps + warp;
@@ -231,7 +314,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32)
     for (int s = 0; s < kStreamStages; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
-  __syncwarp();
+  __syncthreads();  // (the service warp's request barriers are initialised)
   const int n = beg < end ? static_cast<int>(end - beg) : 0;
 
   // the range's position as (window-head, query group, block), advanced without divisions
@@ -271,31 +354,34 @@ __global__ void __launch_bounds__(kStreamWarps * 32)
   long long cur = -1;
   int nblk = 0;
   uint32_t late = 0;  // stages whose wait timed out (their copies may still be in flight)
-  // units this warp flushed and must combine if it turned out to complete them (lane 0 knows), at most two pending
-  long long pend_u0 = -1, pend_u1 = -1;
-  int pend_l0 = 0, pend_l1 = 0;
-  auto flush = [&](long long u, int nb) {
-    const int last = write_partial<NT>(st, a, u, nb, gw, lane);
-    if (pend_u0 < 0) {
-      pend_u0 = u;
-      pend_l0 = last;
-    } else {
-      if (pend_u1 >= 0) {  // (a third unit: settle the oldest now)
-        if (__shfl_sync(0xffffffffu, pend_l0, 0)) combine_unit<T, NT>(a, pend_u0, lane);
-        pend_u0 = pend_u1;
-        pend_l0 = pend_l1;
-      }
-      pend_u1 = u;
-      pend_l1 = last;
-    }
-  };
+  // Only a range's first unit (when it began in an earlier warp's range) and its last one (when it goes on into the
+  // next warp's range) are shared with other warps: they go through partials and the units' counters; a unit wholly
+  // inside the range goes straight to the output from registers. The first unit, when the range goes on past it, is
+  // handed to the CTA's service warp once its partial is stored: an mbarrier arrival (a CTA-scope release) instead of
+  // the GPU-scope fence a count needs, which would stall this warp -- with its loads in flight -- for about as long
+  // as eight blocks take to stream (measured). The last unit is counted by this warp at the end of its range.
+  const bool first_shared = beg % a.bpu != 0;
+  if (!(n > 0 && first_shared && beg + n > (u0 + 1) * a.bpu) && lane == 0) {  // no such unit: say so
+    req_u[warp] = -1;
+    mbar_arrive(&req_bar[warp]);
+  }
   int c_wh = static_cast<int>(u0 / a.QG), c_qg = static_cast<int>(u0 % a.QG);
   int c_b = static_cast<int>(beg - u0 * a.bpu);
   long long c_u = u0;
   for (int j = 0; j < n;) {
     if (c_u != cur) {
       if (cur >= 0) {
-        flush(cur, nblk);
+        if (cur == u0 && first_shared) {
+          store_partial<NT>(st, a, cur, gw, lane);
+          __syncwarp();  // (every lane's stores before lane 0's arrival)
+          if (lane == 0) {
+            req_u[warp] = cur;
+            req_n[warp] = nblk;
+            mbar_arrive(&req_bar[warp]);
+          }
+        } else {
+          finalize_unit<T, NT>(st, a, cur, lane);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -362,9 +448,17 @@ __global__ void __launch_bounds__(kStreamWarps * 32)
       }
     }
   }
-  if (cur >= 0) flush(cur, nblk);
-  if (pend_u0 >= 0 && __shfl_sync(0xffffffffu, pend_l0, 0)) combine_unit<T, NT>(a, pend_u0, lane);
-  if (pend_u1 >= 0 && __shfl_sync(0xffffffffu, pend_l1, 0)) combine_unit<T, NT>(a, pend_u1, lane);
+  // the last unit: shared if it began before the range or goes on after it (the loop did not step past its last block)
+  const bool last_shared = cur >= 0 && ((cur == u0 && first_shared) || c_u == cur);
+  if (cur >= 0) {
+    if (last_shared)
+      store_partial<NT>(st, a, cur, gw, lane);
+    else
+      finalize_unit<T, NT>(st, a, cur, lane);
+  }
+  if (last_shared) {
+    if (__shfl_sync(0xffffffffu, publish(a, cur, nblk, lane) ? 1 : 0, 0)) combine_unit<T, NT>(a, cur, lane);
+  }
   // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
   for (int j = n - min(n, kStreamStages); j < n; ++j) {
     const int s = j % kStreamStages;
@@ -420,16 +514,16 @@ StreamPlan plan_stream(int W, int S, int H, int Tn) {
   return p;
 }
 
-template <typename T, int NT, int WARPS, int STAGES, bool PAIR>
+template <typename T, int NT, int WARPS, int STAGES, bool PAIR, int CTAS>
 int launch_stream_shape(const CUtensorMap &km, const CUtensorMap &vm, const StreamArgs &a, int grid, void *stream) {
   constexpr int smem = smem_bytes(WARPS, STAGES);
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(cross_stream_kernel<T, NT, WARPS, STAGES, PAIR>,
+    cudaFuncSetAttribute(cross_stream_kernel<T, NT, WARPS, STAGES, PAIR, CTAS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr = true;
   }
-  return launch("cross_attn", cross_stream_kernel<T, NT, WARPS, STAGES, PAIR>, dim3(grid), dim3(WARPS * 32), smem,
+  return launch("cross_attn", cross_stream_kernel<T, NT, WARPS, STAGES, PAIR, CTAS>, dim3(grid), dim3((WARPS + 1) * 32), smem,
                 stream, km, vm, a);
 }
 
@@ -437,12 +531,12 @@ template <typename T, int NT>
 int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamArgs &a, int grid, int shape,
                      void *stream) {
   if constexpr (NT >= 2) {  // (more query tiles: shape 0 only)
-    return launch_stream_shape<T, NT, kShapes[0].warps, kShapes[0].stages, kShapes[0].pair>(km, vm, a, grid, stream);
+    return launch_stream_shape<T, NT, kShapes[0].warps, kShapes[0].stages, kShapes[0].pair, kShapes[0].ctas>(km, vm, a, grid, stream);
   } else {
     switch (shape) {
 #define WT_SHAPE_CASE(i)                                                                                      \
   case i:                                                                                                    \
-    return launch_stream_shape<T, NT, kShapes[i].warps, kShapes[i].stages, kShapes[i].pair>(km, vm, a, grid, \
+    return launch_stream_shape<T, NT, kShapes[i].warps, kShapes[i].stages, kShapes[i].pair, kShapes[i].ctas>(km, vm, a, grid, \
                                                                                              stream);
       WT_SHAPE_CASE(0)
       WT_SHAPE_CASE(1)
@@ -450,7 +544,7 @@ int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamA
       WT_SHAPE_CASE(4)
 #undef WT_SHAPE_CASE
       default:
-        return launch_stream_shape<T, NT, kShapes[2].warps, kShapes[2].stages, kShapes[2].pair>(km, vm, a, grid,
+        return launch_stream_shape<T, NT, kShapes[2].warps, kShapes[2].stages, kShapes[2].pair, kShapes[2].ctas>(km, vm, a, grid,
                                                                                                stream);
     }
   }
