@@ -11,24 +11,26 @@
 //     (so no key load waits on an index load) and its warps take 4 contiguous quarters of the keys, so the longest
 //     row's chain of dependent loads is a quarter as long as with one warp per (row, head), and the many short
 //     CTAs balance over the SMs by themselves;
-//   * each warp streams 16-key stages through a 2-deep cp.async ring (16-byte copies, bypassing L1): the loads in
+//   * each warp streams stages of 4 * U keys through an S-deep cp.async ring (16-byte copies, bypassing L1; head_dim
+//     64 with up to 256 slots per split: U = 2, S = 3, 24 KB of rings per CTA keep 8 CTAs on an SM; else U = 4,
+//     S = 2): the loads in
 //     flight hold no registers, and the ring is laid out chunk-major ([chunk][lane]) so every read-back is bank-
 //     conflict free;
 //   * a key row is covered by D/8 lanes (one 16-byte piece each), dot products on mixed-precision FMAs (half/bf16
 //     products accumulated in fp32) finished with butterfly shuffles; each group of D/8 lanes runs its own online
-//     softmax (4 keys per stage); groups merge by shuffles, the 4 warps through shared memory;
+//     softmax (U keys per stage); groups merge by shuffles, the 4 warps through shared memory;
 //   * kv_splits > 1 splits the cache capacity into equal static ranges; each split writes its partial (acc, m, l)
 //     to the workspace and the last CTA of the (row, head) -- an atomic counter, no waiting -- combines them;
 //   * with programmatic dependent launch the offset, slot table and cache reads start before the preceding kernel
 //     has finished (only the new token's q/k/v wait for it).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace wt {
 namespace {
 
 constexpr int kWarpsPerCta = 4;  // key quarters of one (row, head)
-constexpr int kStages = 2;       // cp.async ring depth per warp (stages of 16 keys)
-constexpr int kKeysPerGroup = 4;
 constexpr int kMaxSplitKeys = 1024;  // cache slots per (row, head, split) staged in shared memory
 
 __device__ __forceinline__ float ex2(float x) {
@@ -100,17 +102,18 @@ __device__ __forceinline__ void merge_state(float &m, float &l, float (&acc)[8],
   m = mn;
 }
 
-// shared memory: per warp a ring ([stage][2 * 4 chunks][32 lanes] x 16 bytes), then the CTA's staged source rows
-constexpr int kRingBytes = kStages * 2 * kKeysPerGroup * 32 * 16;
+// shared memory: per warp a ring ([stage][2 * U chunks][32 lanes] x 16 bytes), then the CTA's staged source rows
+template <int U, int S>
+constexpr int ring_bytes() { return S * 2 * U * 32 * 16; }
 
-template <typename T, int D>
+template <typename T, int D, int U, int kStages>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
     self_step_kernel(const T *__restrict__ qkv, T *kc, T *vc, const int64_t *__restrict__ offset,
                      const int32_t *__restrict__ src, T *__restrict__ y, float *__restrict__ part,
                      int *__restrict__ counters, int N, int H, int C, int write_cache, int splits, float scale) {
   constexpr int LPK = D / 8;     // lanes per key row (16 bytes each)
   constexpr int GPW = 32 / LPK;  // key groups per warp
-  constexpr int U = kKeysPerGroup;
+  constexpr int kRingBytes = ring_bytes<U, kStages>();
   constexpr int KPS = GPW * U;   // keys per stage
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -322,12 +325,12 @@ size_t step_workspace(int rows, int heads, int head_dim, int splits) {
   return counters + static_cast<size_t>(rows) * heads * splits * (head_dim + 2) * sizeof(float);
 }
 
-template <typename T, int D>
+template <typename T, int D, int U, int kStages>
 int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y, int N,
                 int H, int C, int write_cache, int splits, void *ws, void *stream) {
   const int cap = (C + splits - 1) / splits;
-  const int smem = kWarpsPerCta * kRingBytes + (cap * 4 + 15) / 16 * 16;
-  auto kernel = self_step_kernel<T, D>;
+  const int smem = kWarpsPerCta * ring_bytes<U, kStages>() + (cap * 4 + 15) / 16 * 16;
+  auto kernel = self_step_kernel<T, D, U, kStages>;
   static int attr_bytes = 0;
   if (smem > attr_bytes) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -346,14 +349,37 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
                 static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale);
 }
 
+// Ring shape (keys per lane group per stage, stages) of the head_dim 64 kernel. By default it follows the cache
+// slots per split: up to 256, (2, 3) -- 24 KB of rings per CTA keep 8 CTAs on an SM while 16 keys per warp are in
+// flight before the wait for the preceding kernel (measured per step: 1980 -> 1924 us at 160 rows, C 228; 670 ->
+// 666 us at 40 rows); above, (4, 2) -- long rows want 32 keys per warp in flight (1589 us at 80 rows, C 448, lengths
+// U[224, 447], against 1674 with (2, 3)). WT_SELF_SHAPE (a tuning knob) forces 0 = (4, 2), 1 = (2, 2), 2 = (2, 3) or
+// 3 = (1, 4).
+int self_shape(int cap) {
+  static int forced = -2;
+  if (forced == -2) {
+    const char *e = getenv("WT_SELF_SHAPE");
+    const int x = e ? atoi(e) : -1;
+    forced = (x >= 0 && x <= 3) ? x : -1;
+  }
+  if (forced >= 0) return forced;
+  return cap <= 256 ? 2 : 0;
+}
+
 template <typename T>
 int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y,
                   int N, int H, int C, int write_cache, int splits, void *ws, void *stream) {
   switch (D) {
-    case 16: return launch_step<T, 16>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-    case 32: return launch_step<T, 32>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-    case 64: return launch_step<T, 64>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-    case 128: return launch_step<T, 128>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+    case 16: return launch_step<T, 16, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+    case 32: return launch_step<T, 32, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+    case 64:
+      switch (self_shape((C + splits - 1) / splits)) {
+        case 1: return launch_step<T, 64, 2, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+        case 3: return launch_step<T, 64, 1, 4>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+        case 2: return launch_step<T, 64, 2, 3>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+        default: return launch_step<T, 64, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+      }
+    case 128: return launch_step<T, 128, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
     default: return fail(WT_ERR_UNSUPPORTED, "self_attn_step: head_dim %d (supported: 16, 32, 64, 128)", D);
   }
 }

@@ -155,14 +155,14 @@ def main() -> None:
     p.add_argument("--d-model", type=int, default=1280)
     p.add_argument("--tokens", type=int, default=224)
     p.add_argument("--cached", type=int, default=0)
-    p.add_argument("--capacity", type=int, default=448)
+    p.add_argument("--capacity", type=int, default=None, help="cache capacity (default: 448 prompt, 228 self_step)")
     p.add_argument("--cache-lo", type=int, default=4)
     p.add_argument("--cache-hi", type=int, default=224)
     p.add_argument("--reps", type=int, default=20)
     a = p.parse_args()
     assert torch.cuda.is_available(), "needs a CUDA GPU"
-    if a.kernel == "self_step" and a.capacity == 448:
-        a.capacity = 228
+    if a.capacity is None:
+        a.capacity = 228 if a.kernel == "self_step" else 448
     print(json.dumps(globals()[a.kernel](a)))
 
 
