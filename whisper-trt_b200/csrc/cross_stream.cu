@@ -37,15 +37,18 @@ constexpr int kErrTimeout = 1;
 constexpr int kPart = kD + 4;  // floats per query of a partial: acc[64], m, l, 2 pad (16-byte aligned records)
 
 // Launch shapes: streaming warps per CTA (plus the service warp) x ring stages per warp x CTAs per SM. Shared
-// memory: warps * stages * 4 KB per CTA. Default: 5 (+1) warps x 5 stages, 2 CTAs per SM: 10 streaming warps and
-// 200 KB of ring per SM (before the service warp: 6 warps x 4 stages x 2 CTAs measured best at 8 and 32 windows;
-// 4x6, 3x8, 5x5 x 2 CTAs and 12x4 x 1 CTA were slower).
+// memory: warps * stages * 4 KB per CTA. Small problems (under 24 blocks per warp with shape 2) take shape 2,
+// 5 (+1) warps x 5 stages x 2 CTAs: 10 streaming warps and 200 KB of ring per SM; larger ones shape 5, 3 (+1) warps
+// x 8 stages x 2 CTAs: fewer, longer ranges (fewer partials per (window, head)) with the same bytes in flight.
+// Measured (us per launch / per config step): 8 windows 20.1 (shape 2) vs 20.6 (shape 5); 32 windows 49.5 vs 48.5,
+// step 1919 vs 1911; 64 windows step 4680 vs 4567. 5 x 9 x 1 CTA and 8 x 6 x 1 CTA were slower at both sizes.
 struct Shape {
   int warps, stages;
   bool pair;  // two 16-key blocks per step of the online softmax
   int ctas;   // CTAs per SM
 };
-constexpr Shape kShapes[] = {{11, 4, false, 1}, {11, 4, true, 1}, {5, 5, true, 2}, {5, 4, true, 2}, {11, 5, true, 1}};
+constexpr Shape kShapes[] = {{11, 4, false, 1}, {11, 4, true, 1}, {5, 5, true, 2},
+                             {5, 4, true, 2},   {11, 5, true, 1}, {3, 8, true, 2}};
 
 constexpr int smem_bytes(int warps, int stages) {
   return warps * stages * kStageBytes + warps * stages * 8 + warps * 24 + 1024;
@@ -479,13 +482,13 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
-// The launch shape: kShapes[WT_CROSS_SHAPE] if that environment variable is set (a tuning knob), else the default.
-int shape_index() {
-  static int idx = -1;
-  if (idx < 0) {
+// A launch shape forced by the WT_CROSS_SHAPE environment variable (a tuning knob), or -1.
+int forced_shape() {
+  static int idx = -2;
+  if (idx == -2) {
     const char *e = getenv("WT_CROSS_SHAPE");
-    int v = e ? atoi(e) : 2;
-    idx = (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : 2;
+    const int v = e ? atoi(e) : -1;
+    idx = (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : -1;
   }
   return idx;
 }
@@ -503,7 +506,14 @@ StreamPlan plan_stream(int W, int S, int H, int Tn) {
   p.bpu = (Tn + 15) / 16;
   p.units = static_cast<long long>(W) * H * p.qgs;
   p.total = p.units * p.bpu;
-  p.shape = p.nt >= 2 ? 0 : shape_index();  // (more query tiles: one block per step keeps them in registers)
+  if (p.nt >= 2) {
+    p.shape = 0;  // (more query tiles: one block per step keeps them in registers)
+  } else if (forced_shape() >= 0) {
+    p.shape = forced_shape();
+  } else {
+    const long long w2 = static_cast<long long>(sm_count()) * kShapes[2].ctas * kShapes[2].warps;
+    p.shape = (p.total + w2 - 1) / w2 >= 24 ? 5 : 2;
+  }
   p.grid = sm_count() * kShapes[p.shape].ctas;
   const long long warps = static_cast<long long>(p.grid) * kShapes[p.shape].warps;
   p.per_warp = (p.total + warps - 1) / warps;
@@ -542,6 +552,7 @@ int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamA
       WT_SHAPE_CASE(1)
       WT_SHAPE_CASE(3)
       WT_SHAPE_CASE(4)
+      WT_SHAPE_CASE(5)
 #undef WT_SHAPE_CASE
       default:
         return launch_stream_shape<T, NT, kShapes[2].warps, kShapes[2].stages, kShapes[2].pair, kShapes[2].ctas>(km, vm, a, grid,
