@@ -200,6 +200,32 @@ int wt_beam_scores(const float *logits, const uint8_t *suppress, const uint8_t *
                    int no_speech, int no_timestamps, int ts_begin, int eot, void *workspace, size_t workspace_bytes,
                    void *stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * The decoder step's linear layers with their LayerNorm, bias, GELU and residual fused around them, on the
+ * 5th-generation tensor cores (tcgen05); x [rows, in], w [out, in] (nn.Linear layout), b [out], all of one 16-bit
+ * type (fp16 or bf16); fp32 accumulation; in and out multiples of 8.
+ * wt_layer_norm_bias replaces decoder_kernels.py:127-135 layer_norm_bias (kernel :100-115):
+ *   y [rows, d] = LN(x) (fp32 statistics: mean, then the mean square of x - mean; rstd = 1/sqrt(var + eps);
+ *   rounded), and x = x + bias in place (after it is read).
+ * wt_ln_linear replaces decoder_kernels.py:138-146 ln_linear (kernel :42-75):
+ *   y [rows, out] = LN(x) . w^T + b, rounded to the 16-bit type (LN(x) rounded first); gelu != 0: y =
+ *   round(gelu(round(...))) with gelu(v) = v/2 (1 + erf(v / sqrt 2)) in fp32.
+ * wt_linear_residual replaces decoder_kernels.py:149-157 linear_residual (kernel :77-97):
+ *   y [rows, out] = round(round(x . w^T + b) + res); y may be res (the residual stream updated in place).
+ *   Both GEMMs need a workspace of wt_dec_linear_workspace(rows, out, in, layer_norm) bytes (layer_norm: 1 for
+ *   wt_ln_linear, 0 for wt_linear_residual; it depends on the device's SM count), zeroed before its first use and
+ *   left with its counters zeroed by each call; its first 4 bytes are a device error word (non-zero after a bounded
+ *   wait gave up). Calls that may overlap on the GPU must not share a workspace.
+ * ------------------------------------------------------------------------------------------------------- */
+size_t wt_dec_linear_workspace(int rows, int out_features, int in_features, int layer_norm);
+int wt_layer_norm_bias(int dtype, void *x, const void *gamma, const void *beta, const void *bias, void *y, int rows,
+                       int d, float eps, void *stream);
+int wt_ln_linear(int dtype, const void *x, const void *gamma, const void *beta, const void *w, const void *b, void *y,
+                 int rows, int out_features, int in_features, int gelu, float eps, void *workspace,
+                 size_t workspace_bytes, void *stream);
+int wt_linear_residual(int dtype, const void *x, const void *w, const void *b, const void *res, void *y, int rows,
+                       int out_features, int in_features, void *workspace, size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

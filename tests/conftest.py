@@ -39,3 +39,10 @@ def slots_golden():
     import numpy as np
 
     return np.load(ROOT / "tests" / "golden" / "slots_golden.npz")
+
+
+@pytest.fixture(scope="session")
+def decoder_golden():
+    import numpy as np
+
+    return np.load(ROOT / "tests" / "golden" / "decoder_golden.npz")

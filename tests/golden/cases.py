@@ -105,3 +105,29 @@ def make_attn_inputs(kind: str, kw: dict) -> dict:
 
 def inputs_digest(inp: dict) -> str:
     return digest(*[inp[k] for k in sorted(inp)])
+
+
+# --- the decoder step's fused linear layers (decoder_kernels.py) -------------------------------------------------
+def linear_case(m=5, n=128, k=64, seed=3):
+    """Inputs of one fused linear layer: x ~ N(0,1) [m, k], LN gamma ~ 1 + N(0,1)*0.1, beta ~ N(0,1)*0.1 [k],
+    w ~ N(0,1)*0.02 [n, k] (nn.Linear layout), b ~ N(0,1)*0.02 [n], residual ~ N(0,1) [m, n], a bias for
+    layer_norm_bias ~ N(0,1)*0.02 [k]; all fp16."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(m, k, generator=g).half()
+    gamma = (1 + 0.1 * torch.randn(k, generator=g)).half()
+    beta = (0.1 * torch.randn(k, generator=g)).half()
+    w = (0.02 * torch.randn(n, k, generator=g)).half()
+    b = (0.02 * torch.randn(n, generator=g)).half()
+    res = torch.randn(m, n, generator=g).half()
+    bias = (0.02 * torch.randn(k, generator=g)).half()
+    return {"x": x, "gamma": gamma, "beta": beta, "w": w, "b": b, "res": res, "bias": bias}
+
+
+# name -> linear_case kwargs: rows 1 / 5 / 40 (a token, a window of beam 5, config 2's 40 rows), a multi-tile
+# feature count, ragged k blocks (k = 200: 64-element blocks with a partial last one) and whisper's d = 1280
+DEC_CASES = {
+    "row1": dict(m=1, n=128, k=64, seed=3),
+    "beam5": dict(m=5, n=384, k=200, seed=4),
+    "rows40": dict(m=40, n=256, k=1280, seed=5),
+    "rows17_wide": dict(m=17, n=1280, k=256, seed=6),
+}

@@ -5,8 +5,9 @@ Run where the reference source tree is importable (it does not travel to the GPU
 
     python tests/golden/make_golden.py [--reference-src <path to the reference's src/ directory>]
 
-Writes ``attn_golden.npz`` (attention outputs + input digests) and ``slots_golden.npz`` (per-step search states
-before/after the reference's bookkeeping) next to this script.
+Writes ``attn_golden.npz`` (attention outputs + input digests), ``slots_golden.npz`` (per-step search states
+before/after the reference's bookkeeping), ``scores_golden.npz`` (beam scoring) and ``decoder_golden.npz`` (the
+fused decoder linear layers; ``--only decoder`` writes just this one) next to this script.
 """
 
 from __future__ import annotations
@@ -241,11 +242,46 @@ def scores_golden(ref_src: str) -> dict:
     return out
 
 
+def decoder_golden(ref_src: str) -> dict:
+    """The fused linear layers of decoder_kernels.py as the reference's own modules compute them on CPU:
+    ``modeling.LayerNorm`` (fp32 statistics with ``Precision.ln32``, rounded to fp16), ``modeling.gelu`` (fp32 with
+    ``Precision.gelu32``), and the GEMM in fp32 rounded to fp16 before the GELU / residual (the rounding points the
+    module's docstring states, decoder_kernels.py:1-15)."""
+    from whisper_trt import modeling
+
+    modeling.Precision.ln32 = True
+    modeling.Precision.gelu32 = True
+    out = {}
+    for name, kw in cases.DEC_CASES.items():
+        inp = cases.linear_case(**kw)
+        out[f"{name}/digest"] = np.array(cases.digest(*[inp[k] for k in sorted(inp)]))
+        k = inp["x"].shape[1]
+        ln = modeling.LayerNorm(k).half()
+        with torch.no_grad():
+            ln.weight.copy_(inp["gamma"])
+            ln.bias.copy_(inp["beta"])
+            xn = ln(inp["x"])  # fp16
+            h = (xn.float() @ inp["w"].float().t() + inp["b"].float()).half()
+            out[f"{name}/ln_linear"] = h.numpy()
+            out[f"{name}/ln_linear_gelu"] = modeling.gelu(h).numpy()
+            g = (inp["x"].float() @ inp["w"].float().t() + inp["b"].float()).half()
+            out[f"{name}/linear_residual"] = (g.float() + inp["res"].float()).half().numpy()
+            out[f"{name}/layer_norm"] = xn.numpy()
+            out[f"{name}/x_plus_bias"] = (inp["x"].float() + inp["bias"].float()).half().numpy()
+    return out
+
+
 def main() -> None:
     ap_ = argparse.ArgumentParser()
     ap_.add_argument("--reference-src", default="/root/reference/src")
+    ap_.add_argument("--only", choices=["decoder"], default=None, help="write only this fixture")
     args = ap_.parse_args()
     sys.path.insert(0, args.reference_src)
+    if args.only == "decoder":
+        d = decoder_golden(args.reference_src)
+        np.savez_compressed(HERE / "decoder_golden.npz", **d)
+        print(f"decoder cases: {len(cases.DEC_CASES)}")
+        return
     from whisper_trt import attn_plugin
 
     attn_plugin.RUNTIME_TRITON = False
@@ -256,6 +292,7 @@ def main() -> None:
     np.savez_compressed(HERE / "slots_golden.npz", **s)
     sc = scores_golden(args.reference_src)
     np.savez_compressed(HERE / "scores_golden.npz", **sc)
+    np.savez_compressed(HERE / "decoder_golden.npz", **decoder_golden(args.reference_src))
     print(f"attn cases: {len(cases.ATTN_CASES)}; bookkeeping steps: {sum(k.endswith('/meta') for k in s)}; "
           f"scoring steps: {sum(k.endswith('/meta') for k in sc)}")
 

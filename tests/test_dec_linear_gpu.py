@@ -1,0 +1,151 @@
+"""GPU parity of the fused decoder linear layers (whisper_trt_b200.decoder_kernels -> the C ABI's
+wt_layer_norm_bias / wt_ln_linear / wt_linear_residual) against the oracle (oracle/decoder.py, pinned to the
+reference's modules) and against the reference fixtures directly.
+
+Tolerance: the outputs are 16-bit; the kernels' fp32 sums run in another order than the oracle's, so an output may
+land one unit in the last place away (2^-10 relative in fp16, 2^-7 in bf16) -- rtol/atol below -- and the large
+majority must be bit-identical."""
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import decoder as od
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f16": (2e-3, 2e-3, 0.9), "bf16": (1.6e-2, 1.6e-2, 0.85)}  # rtol, atol, bit-identical fraction at least
+
+
+def _dk():
+    from whisper_trt_b200 import decoder_kernels
+
+    return decoder_kernels
+
+
+def _make(m, n, k, dtype, seed):
+    inp = cases.linear_case(m=m, n=n, k=k, seed=seed)
+    return {key: v.to(dtype).cuda() for key, v in inp.items()}
+
+
+def _f(t):
+    return t.float().cpu().numpy()
+
+
+def _check(got, want, dt):
+    rtol, atol, frac = TOL[dt]
+    got = _f(got)
+    np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+    assert np.mean(got == want) >= frac, np.mean(got == want)
+
+
+SHAPES = [(1, 128, 64), (5, 384, 200), (40, 1280, 1280), (160, 3840, 1280), (160, 5120, 1280), (160, 1280, 5120),
+          (300, 1280, 1280), (33, 136, 72)]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("gelu", [False, True])
+def test_ln_linear(m, n, k, gelu):
+    dk = _dk()
+    t = _make(m, n, k, torch.float16, seed=m + n + k)
+    y = dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"], t["b"], gelu=gelu)
+    torch.cuda.synchronize()
+    want = od.ln_linear(_f(t["x"]), _f(t["gamma"]), _f(t["beta"]), _f(t["w"]), _f(t["b"]), gelu_=gelu)
+    _check(y, want, "f16")
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_linear_residual(m, n, k):
+    dk = _dk()
+    t = _make(m, n, k, torch.float16, seed=2 * (m + n + k))
+    want = od.linear_residual(_f(t["x"]), _f(t["w"]), _f(t["b"]), _f(t["res"]))
+    y = dk.linear_residual(t["x"], t["w"], t["b"], t["res"])
+    _check(y, want, "f16")
+    # in place: the residual stream updated (out = res), as the decoder step calls it
+    dk.linear_residual(t["x"], t["w"], t["b"], t["res"], out=t["res"])
+    _check(t["res"], want, "f16")
+
+
+@pytest.mark.parametrize("m,k", [(1, 64), (5, 200), (160, 1280), (300, 5120)])
+def test_layer_norm_bias(m, k):
+    dk = _dk()
+    t = _make(m, 8, k, torch.float16, seed=m + k)
+    x0 = _f(t["x"])
+    y = dk.layer_norm_bias(t["x"], t["gamma"], t["beta"], t["bias"])
+    want_y, want_x = od.layer_norm_bias(x0, _f(t["gamma"]), _f(t["beta"]), _f(t["bias"]))
+    _check(y, want_y, "f16")
+    np.testing.assert_array_equal(_f(t["x"]), want_x)  # (x + bias: one rounding, exact)
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 384, 200), (160, 1280, 1280)])
+def test_bf16(m, n, k):
+    dk = _dk()
+    t = _make(m, n, k, torch.bfloat16, seed=7)
+    f = {key: _f(v) for key, v in t.items()}
+    y = dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"], t["b"], gelu=True)
+    _check(y, od.ln_linear(f["x"], f["gamma"], f["beta"], f["w"], f["b"], gelu_=True, dt="bf16"), "bf16")
+    z = dk.linear_residual(t["x"], t["w"], t["b"], t["res"])
+    _check(z, od.linear_residual(f["x"], f["w"], f["b"], f["res"], dt="bf16"), "bf16")
+
+
+@pytest.mark.parametrize("name", list(cases.DEC_CASES))
+def test_reference_fixtures(name, decoder_golden):
+    """Straight against the reference's own outputs (not through the oracle)."""
+    dk = _dk()
+    inp = cases.linear_case(**cases.DEC_CASES[name])
+    t = {k: v.cuda() for k, v in inp.items()}
+    _check(dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"], t["b"]),
+           decoder_golden[f"{name}/ln_linear"].astype(np.float32), "f16")
+    _check(dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"], t["b"], gelu=True),
+           decoder_golden[f"{name}/ln_linear_gelu"].astype(np.float32), "f16")
+    _check(dk.linear_residual(t["x"], t["w"], t["b"], t["res"]),
+           decoder_golden[f"{name}/linear_residual"].astype(np.float32), "f16")
+
+
+def test_repeated_calls_and_graph_capture():
+    """Calls of one shape reuse a workspace (each leaves its counters zeroed); a captured sequence replays."""
+    dk = _dk()
+    t = _make(160, 1280, 1280, torch.float16, seed=11)
+    want = od.linear_residual(_f(t["x"]), _f(t["w"]), _f(t["b"]), _f(t["res"]))
+    for _ in range(3):
+        _check(dk.linear_residual(t["x"], t["w"], t["b"], t["res"]), want, "f16")
+    res0 = t["res"].clone()
+    out = torch.empty_like(res0)
+    q = dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"], t["b"])  # (workspace allocated before capture)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        dk.linear_residual(t["x"], t["w"], t["b"], res0, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"], t["b"], out=q)
+        dk.linear_residual(t["x"], t["w"], t["b"], res0, out=out)
+    for _ in range(2):
+        q.zero_()
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        _check(out, want, "f16")
+        _check(q, od.ln_linear(_f(t["x"]), _f(t["gamma"]), _f(t["beta"]), _f(t["w"]), _f(t["b"])), "f16")
+
+
+def test_bad_shapes_raise():
+    dk = _dk()
+    t = _make(5, 128, 64, torch.float16, seed=1)
+    with pytest.raises(ValueError):
+        dk.ln_linear(t["x"], t["gamma"], t["beta"], t["w"][:, :32], t["b"])
+    with pytest.raises(ValueError):
+        dk.linear_residual(t["x"], t["w"], t["b"], t["res"][:, :64])
+    with pytest.raises(ValueError):  # (in_features not a multiple of 8: the C ABI refuses it)
+        x = torch.randn(5, 60, device="cuda").half()
+        w = torch.randn(128, 60, device="cuda").half()
+        dk.linear_residual(x, w, t["b"], t["res"])
+
+
+def test_no_device_errors_recorded():
+    from whisper_trt_b200 import attn_plugin as ap
+
+    torch.cuda.synchronize()
+    assert ap.workspace_errors() == 0

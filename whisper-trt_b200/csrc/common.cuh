@@ -55,6 +55,34 @@ int launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   return WT_OK;
 }
 
+// The same with thread-block clusters of `cluster_x` CTAs along x (gridDim.x a multiple of it).
+template <typename... KArgs, typename... Args>
+int launch_clustered(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,
+                     int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (launch_flags() & WT_LAUNCH_PDL) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return fail(WT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return WT_OK;
+}
+
 // ---- device side -----------------------------------------------------------------------------------------
 // Programmatic dependent launch controls (no-ops when the kernel was launched without the attribute). The kernels
 // trigger their dependents right after their own wait: a dependent then starts while this kernel works, but no

@@ -1,0 +1,569 @@
+// The decoder step's linear layers with their LayerNorm, bias, GELU and residual fused around them -- the reference's
+// decoder_kernels.py (ln_linear :138-146 / kernel :42-75, linear_residual :149-157 / kernel :77-97, layer_norm_bias
+// :127-135 / kernel :100-115), as the step calls them (runtime.py:134-151):
+//   layer_norm_bias: y = LN(x) (fp32 statistics: mean, then the mean square of x - mean; rounded to the input type)
+//                    and, in place, x = x + bias;
+//   ln_linear:       y = LN(x) . w^T + b (fp32 accumulation), rounded; with GELU, gelu(rounded) in fp32, rounded;
+//   linear_residual: y = round(round(x . w^T + b) + res), res and y may be the same tensor.
+//
+// B200 design. At a decode step the rows (1-320) are few and every GEMM streams its weights once: HBM-bound,
+// short, and with too few 128-feature output tiles (10-40) to occupy 148 SMs. So:
+//   * one tcgen05 kernel, one unit per CTA: a unit is (row chunk of <= 256, 128-feature tile, k split); the weights
+//     are the MMA's A (M = 128 features), the rows its B (N = rows, padded to 16), 64-element k blocks staged by
+//     TMA (128-byte swizzle) through a ring; warp 0 issues the loads, warp 1 the MMAs into a tensor-memory
+//     accumulator, warps 2-5 the epilogue;
+//   * the k range of a tile is split over the CTAs of a thread-block cluster (up to 8, enough to occupy the SMs):
+//     each CTA parks its fp32 partial in its own shared memory (the ring, idle once its MMAs are done), and after
+//     a cluster barrier each CTA sums its share of the tile's rows over all the cluster's partials through
+//     distributed shared memory, in split order (the same sums whichever CTA finishes first), and applies the
+//     fused epilogue -- no partial leaves the chip;
+//   * ln_linear first normalizes the rows into the workspace with a row kernel; the GEMM is launched after it with
+//     programmatic dependent launch and issues its first stages' weight loads before waiting for it (the weights
+//     are not its output), so the weight stream overlaps the LayerNorm;
+//   * every mbarrier wait is bounded (a timeout records an error in the workspace's device word and the kernel goes
+//     on, then frees its tensor memory).
+#include <cstdlib>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "tc05.cuh"
+#include "tma.cuh"
+
+namespace wt {
+namespace {
+
+constexpr int kDlEpiWarps = 4;
+constexpr int kDlThreads = 32 * (2 + kDlEpiWarps);  // producer, MMA issuer, 4 epilogue warps
+constexpr int kDlTileV = 128;    // output features per unit (the MMA's M)
+constexpr int kDlKBlock = 64;    // reduction elements per stage (one 128-byte swizzled row)
+constexpr int kDlMaxRows = 256;  // rows per unit (the MMA's N, at most 256)
+constexpr int kDlMaxSplits = 8;  // CTAs of a cluster (the portable maximum)
+constexpr int kDlErrTimeout = 1;
+
+enum DlMode { kDlBias = 0, kDlGelu = 1, kDlResidual = 2 };
+
+struct DlArgs {
+  int *err;
+  const void *bias;  // [V]
+  const void *res;   // [N, V] (residual mode)
+  void *y;           // [N, V]
+  int N, V, kblocks, splits, kb_per, vtiles, nmma, tcols, stages, ring_bytes;
+};
+
+struct DlPlan {
+  int chunks, vtiles, kblocks, splits, kb_per, nmma, tcols, stages, stage_bytes, ring_bytes, smem, grid;
+  size_t xn_off, bytes;
+};
+
+// The most k splits a GEMM may take: WT_DL_MAX_SPLITS (a tuning knob), else kDlMaxSplits.
+int max_splits() {
+  static int v = 0;
+  if (v == 0) {
+    const char *e = getenv("WT_DL_MAX_SPLITS");
+    const int x = e ? atoi(e) : kDlMaxSplits;
+    v = (x >= 1 && x <= kDlMaxSplits) ? x : kDlMaxSplits;
+  }
+  return v;
+}
+
+DlPlan dl_plan(int N, int V, int K, bool ln, int sms) {
+  DlPlan p{};
+  p.chunks = (N + kDlMaxRows - 1) / kDlMaxRows;
+  p.vtiles = (V + kDlTileV - 1) / kDlTileV;
+  p.kblocks = (K + kDlKBlock - 1) / kDlKBlock;
+  const int tiles = p.chunks * p.vtiles;
+  int s = sms / tiles;  // splits: enough CTAs for the SMs, at most a cluster, at least 2 k blocks each
+  if (s > kDlMaxSplits) s = kDlMaxSplits;
+  if (s > max_splits()) s = max_splits();
+  if (s > p.kblocks / 2) s = p.kblocks / 2;
+  if (s < 1) s = 1;
+  p.kb_per = (p.kblocks + s - 1) / s;
+  p.splits = (p.kblocks + p.kb_per - 1) / p.kb_per;  // (no empty split)
+  const int nrows = N < kDlMaxRows ? N : kDlMaxRows;
+  p.nmma = (nrows + 15) / 16 * 16;
+  p.tcols = 32;
+  while (p.tcols < p.nmma) p.tcols <<= 1;
+  p.stage_bytes = kDlTileV * 128 + (p.nmma * 128 + 1023) / 1024 * 1024;
+  const int cap = (200 * 1024) / p.stage_bytes < 8 ? (200 * 1024) / p.stage_bytes : 8;
+  p.stages = p.kb_per < cap ? p.kb_per : cap;
+  p.ring_bytes = p.stages * p.stage_bytes;
+  const int part_bytes = p.splits > 1 ? p.nmma * kDlTileV * 4 : 0;  // the partial, parked over the idle ring
+  if (p.ring_bytes < part_bytes) p.ring_bytes = part_bytes;
+  p.smem = 1024 + p.ring_bytes + (2 * p.stages + 2) * 8 + 16;
+  p.grid = tiles * p.splits;
+  p.xn_off = 256;  // [0, 256): the device error word
+  p.bytes = p.xn_off + (ln ? (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256 : 0);
+  return p;
+}
+
+template <typename T>
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
+}
+
+// The fused epilogue of one output element from its fp32 sum, its bias b and (residual mode) its residual r.
+template <typename T, int MODE>
+__device__ __forceinline__ T dl_out(float acc, float b, float r) {
+  const T h = Elem<T>::from_float(acc + b);
+  if (MODE == kDlBias) return h;
+  if (MODE == kDlGelu) return Elem<T>::from_float(gelu_erf<T>(Elem<T>::to_float(h)));
+  return Elem<T>::from_float(Elem<T>::to_float(h) + r);
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const void *p, size_t i) {
+  return Elem<T>::to_float(static_cast<const T *>(p)[i]);
+}
+
+// One unit per CTA: blockIdx.x = tile * splits + split; the splits of a tile are one cluster (rank = split).
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kDlThreads)
+    dec_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                    const DlArgs a) {
+  namespace cg = cooperative_groups;
+  constexpr bool kBF16 = Elem<T>::code == WT_BF16;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int a_bytes = kDlTileV * 128, b_bytes = a.nmma * 128;
+  const int stage_bytes = a_bytes + ((b_bytes + 1023) & ~1023);
+  const int stages = a.stages;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.ring_bytes);
+  uint64_t *empty = full + stages;
+  uint64_t *acc_full = empty + stages;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = a.splits, sp = static_cast<int>(blockIdx.x) % S, t = static_cast<int>(blockIdx.x) / S;
+  const int v0 = (t % a.vtiles) * kDlTileV, n0 = (t / a.vtiles) * kDlMaxRows;
+  const int nn = min(kDlMaxRows, a.N - n0);
+  const int kb0 = sp * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per), nkb = kb1 - kb0;
+
+  if (warp == 0) {
+    tmem_alloc(tmem_holder, static_cast<uint32_t>(a.tcols));
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    prefetch_tensormap(&wmap);
+    prefetch_tensormap(&xmap);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full[0], 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer: this unit's k blocks through the ring
+      // the first stages' weight halves go out before the wait for the preceding kernel (it does not write the
+      // weights); their row halves (possibly its output) after it
+      bool waited = false;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        if (i >= stages) {
+          if (!waited) {
+            pdl_wait();
+            pdl_launch_dependents();
+            for (int j = 0; j < stages; ++j)
+              tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
+            waited = true;
+          }
+          mbar_wait_bounded(&empty[s], ((i / stages) - 1) & 1, a.err, kDlErrTimeout);
+        }
+        unsigned char *st = smem + s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(a_bytes + b_bytes));
+        tma_load_2d(st, &wmap, (kb0 + i) * kDlKBlock, v0, &full[s]);
+        if (waited) tma_load_2d(st + a_bytes, &xmap, (kb0 + i) * kDlKBlock, n0, &full[s]);
+      }
+      if (!waited) {
+        pdl_wait();
+        pdl_launch_dependents();
+        for (int j = 0; j < min(stages, nkb); ++j)
+          tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
+      }
+    } else {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (lane == 0) {  // MMA issuer
+      const uint32_t idesc = idesc_f16(kDlTileV, a.nmma, kBF16);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        mbar_wait_bounded(&full[s], (i / stages) & 1, a.err, kDlErrTimeout);
+        tc_fence_after();
+        const uint32_t a_addr = smem_addr(smem + s * stage_bytes), b_addr = a_addr + a_bytes;
+        const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(b_addr);
+#pragma unroll
+        for (int kk = 0; kk < kDlKBlock / 16; ++kk)  // K = 16 per instruction: +32 bytes along the swizzled row
+          umma_f16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i != 0 || kk != 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&acc_full[0]);
+    }
+  } else {  // epilogue warps: lane quarter warp % 4 = features v0 + 32 (warp % 4) + lane
+    pdl_wait();
+    pdl_launch_dependents();
+    const int quarter = warp & 3;
+    const int v = v0 + quarter * 32 + lane;
+    const float bv = (S == 1 && v < a.V) ? ld_f<T>(a.bias, v) : 0.f;
+    mbar_wait_bounded(&acc_full[0], 0, a.err, kDlErrTimeout);
+    tc_fence_after();
+    const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    T *y = static_cast<T *>(a.y);
+    float *part = reinterpret_cast<float *>(smem);  // [row][128 features], over the idle ring
+    for (int c0 = 0; c0 < a.nmma; c0 += 16) {
+      uint32_t r[16];
+      tmem_ld16(base + static_cast<uint32_t>(c0), r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int n = c0 + q;
+        if (n < nn) {
+          if (S == 1) {
+            if (v < a.V) {
+              const size_t o = static_cast<size_t>(n0 + n) * a.V + v;
+              y[o] = dl_out<T, MODE>(__uint_as_float(r[q]), bv, MODE == kDlResidual ? ld_f<T>(a.res, o) : 0.f);
+            }
+          } else {
+            part[n * kDlTileV + quarter * 32 + lane] = __uint_as_float(r[q]);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  if (S > 1) {
+    // This CTA's share of the tile's rows: the sum of the splits' partials (read from their CTAs' shared memory,
+    // 16 bytes at a time, every split's value of a batch of rows in flight) in split order, then the epilogue.
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every split's partial is in its CTA's shared memory
+    if (warp >= 2) {
+      const int f4 = (tid - 64) & 31, rsub = (tid - 64) >> 5;  // features 4 f4 .. 4 f4 + 3; rows r0 + rsub + 4 i
+      const int rpc = (nn + S - 1) / S, r0 = sp * rpc, r1 = min(nn, r0 + rpc);
+      const float *part = reinterpret_cast<const float *>(smem);
+      const float4 *peer[kDlMaxSplits];
+#pragma unroll
+      for (int s2 = 0; s2 < kDlMaxSplits; ++s2)
+        peer[s2] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(part, s2 < S ? s2 : 0));
+      float bv4[4], rs[4][4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) bv4[e] = v0 + 4 * f4 + e < a.V ? ld_f<T>(a.bias, v0 + 4 * f4 + e) : 0.f;
+      T *y = static_cast<T *>(a.y);
+      constexpr int kR = 4;  // rows per thread per batch
+      for (int n = r0 + rsub; n < r1; n += 4 * kR) {
+        float4 val[kR][kDlMaxSplits];
+#pragma unroll
+        for (int q = 0; q < kR; ++q) {
+          const int row = n + 4 * q;
+#pragma unroll
+          for (int s2 = 0; s2 < kDlMaxSplits; ++s2)
+            val[q][s2] = (s2 < S && row < r1) ? peer[s2][row * (kDlTileV / 4) + f4] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int vv = v0 + 4 * f4 + e;
+            rs[q][e] = (MODE == kDlResidual && row < r1 && vv < a.V)
+                           ? ld_f<T>(a.res, static_cast<size_t>(n0 + row) * a.V + vv) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < kR; ++q) {
+          const int row = n + 4 * q;
+          if (row >= r1) continue;
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int s2 = 0; s2 < kDlMaxSplits; ++s2) {  // in split order (absent splits add +0)
+            acc[0] += val[q][s2].x;
+            acc[1] += val[q][s2].y;
+            acc[2] += val[q][s2].z;
+            acc[3] += val[q][s2].w;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int vv = v0 + 4 * f4 + e;
+            if (vv < a.V) y[static_cast<size_t>(n0 + row) * a.V + vv] = dl_out<T, MODE>(acc[e], bv4[e], rs[q][e]);
+          }
+        }
+      }
+    }
+    cluster.sync();  // (no CTA leaves while another may still read its shared memory)
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(a.tcols));
+}
+
+// LayerNorm of rows of K (a multiple of 8) elements, one warp per row: fp32 statistics (mean, then the mean square of
+// x - mean), y = round((x - mean) * rstd * gamma + beta); with `bias`, x = round(x + bias) in place afterwards.
+// Rows of up to 32 x 8 x kLnRegs elements are read once into registers, gamma / beta / bias loaded alongside
+// (one round trip per row); longer rows take three passes over memory.
+constexpr int kLnRegs = 8;  // 16-byte pieces per lane held in registers: K <= 2048
+template <typename T>
+__global__ void __launch_bounds__(128)
+    ln_rows_kernel(T *x, const T *__restrict__ gamma, const T *__restrict__ beta, const T *__restrict__ bias,
+                   T *__restrict__ y, int N, int K, float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (r >= N) return;
+  T *xr = x + static_cast<size_t>(r) * K;
+  T *yr = y + static_cast<size_t>(r) * K;
+  if (K <= 32 * 8 * kLnRegs) {
+    uint4 xv[kLnRegs], gv[kLnRegs], bv[kLnRegs], cv[kLnRegs];
+#pragma unroll
+    for (int j = 0; j < kLnRegs; ++j) {
+      const int k = (lane + 32 * j) * 8;
+      if (k < K) {
+        xv[j] = *reinterpret_cast<const uint4 *>(xr + k);
+        gv[j] = *reinterpret_cast<const uint4 *>(gamma + k);
+        bv[j] = *reinterpret_cast<const uint4 *>(beta + k);
+        if (bias != nullptr) cv[j] = *reinterpret_cast<const uint4 *>(bias + k);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnRegs; ++j)
+      if ((lane + 32 * j) * 8 < K) {
+        float f[8];
+        unpack8<T>(xv[j], f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s += f[i];
+      }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / K;
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnRegs; ++j)
+      if ((lane + 32 * j) * 8 < K) {
+        float f[8];
+        unpack8<T>(xv[j], f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d = f[i] - mean;
+          v += d * d;
+        }
+      }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float rstd = 1.f / sqrtf(v / K + eps);
+#pragma unroll
+    for (int j = 0; j < kLnRegs; ++j) {
+      const int k = (lane + 32 * j) * 8;
+      if (k < K) {
+        float f[8], g[8], b[8], o[8];
+        unpack8<T>(xv[j], f);
+        unpack8<T>(gv[j], g);
+        unpack8<T>(bv[j], b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = (f[i] - mean) * rstd * g[i] + b[i];
+        *reinterpret_cast<uint4 *>(yr + k) = pack8<T>(o);
+        if (bias != nullptr) {
+          float c[8];
+          unpack8<T>(cv[j], c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] += c[i];
+          *reinterpret_cast<uint4 *>(xr + k) = pack8<T>(f);
+        }
+      }
+    }
+    return;
+  }
+  float s = 0.f;
+  for (int k = lane * 8; k < K; k += 256) {
+    float f[8];
+    unpack8<T>(*reinterpret_cast<const uint4 *>(xr + k), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += f[i];
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / K;
+  float v = 0.f;
+  for (int k = lane * 8; k < K; k += 256) {
+    float f[8];
+    unpack8<T>(*reinterpret_cast<const uint4 *>(xr + k), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = f[i] - mean;
+      v += d * d;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const float rstd = 1.f / sqrtf(v / K + eps);
+  for (int k = lane * 8; k < K; k += 256) {
+    float f[8], g[8], b[8];
+    unpack8<T>(*reinterpret_cast<const uint4 *>(xr + k), f);
+    unpack8<T>(*reinterpret_cast<const uint4 *>(gamma + k), g);
+    unpack8<T>(*reinterpret_cast<const uint4 *>(beta + k), b);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (f[i] - mean) * rstd * g[i] + b[i];
+    *reinterpret_cast<uint4 *>(yr + k) = pack8<T>(o);
+    if (bias != nullptr) {
+      float c[8];
+      unpack8<T>(*reinterpret_cast<const uint4 *>(bias + k), c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] += c[i];
+      *reinterpret_cast<uint4 *>(xr + k) = pack8<T>(f);
+    }
+  }
+}
+
+int g_dl_sm[64] = {};
+int dl_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_dl_sm[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_dl_sm[dev] = n;
+  }
+  return g_dl_sm[dev];
+}
+
+template <typename T, int MODE>
+int launch_gemm(const DlPlan &p, const CUtensorMap &wm, const CUtensorMap &xm, const DlArgs &a, void *stream) {
+  auto kernel = dec_gemm_kernel<T, MODE>;
+  static int attr = 0;
+  if (p.smem > attr) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
+    attr = p.smem;
+  }
+  return launch_clustered("dec_linear", kernel, dim3(p.grid), dim3(kDlThreads), p.smem, stream, p.splits, wm, xm, a);
+}
+
+template <typename T>
+int launch_ln(T *x, const T *gamma, const T *beta, const T *bias, T *y, int N, int K, float eps, void *stream) {
+  return launch("layer_norm", ln_rows_kernel<T>, dim3((N + 3) / 4), dim3(128), 0, stream, x, gamma, beta, bias, y, N,
+                K, eps);
+}
+
+int check_common(const char *what, int dtype, int N, int V, int K) {
+  WT_REQUIRE(N > 0 && V > 0 && K > 0, WT_ERR_ARG, "%s: sizes must be positive (rows %d, out %d, in %d)", what, N, V,
+             K);
+  WT_REQUIRE(K % 8 == 0, WT_ERR_UNSUPPORTED, "%s: in_features %d is not a multiple of 8", what, K);
+  WT_REQUIRE(V % 8 == 0, WT_ERR_UNSUPPORTED, "%s: out_features %d is not a multiple of 8", what, V);
+  WT_REQUIRE(dtype == WT_F16 || dtype == WT_BF16, WT_ERR_DTYPE, "%s: unknown dtype %d", what, dtype);
+  return WT_OK;
+}
+
+// The GEMM with its fused epilogue; `x` its rows (for ln_linear the normalized rows in the workspace).
+int run_gemm(int dtype, int mode, const void *x, const void *w, const void *b, const void *res, void *y, int N,
+             int V, int K, const DlPlan &p, void *workspace, void *stream) {
+  CUtensorMap wm, xm;
+  int st = encode_tile_map(&wm, w, static_cast<unsigned long long>(V), static_cast<unsigned long long>(K), kDlTileV,
+                           dtype);
+  if (st != WT_OK) return st;
+  st = encode_tile_map(&xm, x, static_cast<unsigned long long>(N), static_cast<unsigned long long>(K), p.nmma, dtype);
+  if (st != WT_OK) return st;
+  DlArgs a{reinterpret_cast<int *>(workspace), b, res, y, N, V, p.kblocks, p.splits, p.kb_per, p.vtiles, p.nmma,
+           p.tcols, p.stages, p.ring_bytes};
+  const bool bf = dtype == WT_BF16;
+  switch (mode) {
+    case kDlGelu:
+      return bf ? launch_gemm<__nv_bfloat16, kDlGelu>(p, wm, xm, a, stream) : launch_gemm<__half, kDlGelu>(p, wm, xm, a, stream);
+    case kDlResidual:
+      return bf ? launch_gemm<__nv_bfloat16, kDlResidual>(p, wm, xm, a, stream)
+                : launch_gemm<__half, kDlResidual>(p, wm, xm, a, stream);
+    default:
+      return bf ? launch_gemm<__nv_bfloat16, kDlBias>(p, wm, xm, a, stream) : launch_gemm<__half, kDlBias>(p, wm, xm, a, stream);
+  }
+}
+
+}  // namespace
+}  // namespace wt
+
+extern "C" {
+
+size_t wt_dec_linear_workspace(int rows, int out_features, int in_features, int layer_norm) {
+  if (rows <= 0 || out_features <= 0 || in_features <= 0) return 0;
+  return wt::dl_plan(rows, out_features, in_features, layer_norm != 0, wt::dl_sm_count()).bytes;
+}
+
+int wt_layer_norm_bias(int dtype, void *x, const void *gamma, const void *beta, const void *bias, void *y, int rows,
+                       int d, float eps, void *stream) {
+  using namespace wt;
+  WT_REQUIRE(rows > 0 && d > 0, WT_ERR_ARG, "layer_norm_bias: sizes must be positive (rows %d, d %d)", rows, d);
+  WT_REQUIRE(d % 8 == 0, WT_ERR_UNSUPPORTED, "layer_norm_bias: d %d is not a multiple of 8", d);
+  WT_REQUIRE(x && gamma && beta && bias && y, WT_ERR_ARG, "layer_norm_bias: null pointer");
+  WT_ALIGNED(x);
+  WT_ALIGNED(gamma);
+  WT_ALIGNED(beta);
+  WT_ALIGNED(bias);
+  WT_ALIGNED(y);
+  if (dtype == WT_F16)
+    return launch_ln<__half>(static_cast<__half *>(x), static_cast<const __half *>(gamma),
+                             static_cast<const __half *>(beta), static_cast<const __half *>(bias),
+                             static_cast<__half *>(y), rows, d, eps, stream);
+  if (dtype == WT_BF16)
+    return launch_ln<__nv_bfloat16>(static_cast<__nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(gamma),
+                                    static_cast<const __nv_bfloat16 *>(beta), static_cast<const __nv_bfloat16 *>(bias),
+                                    static_cast<__nv_bfloat16 *>(y), rows, d, eps, stream);
+  return fail(WT_ERR_DTYPE, "layer_norm_bias: unknown dtype %d", dtype);
+}
+
+int wt_ln_linear(int dtype, const void *x, const void *gamma, const void *beta, const void *w, const void *b, void *y,
+                 int rows, int out_features, int in_features, int gelu, float eps, void *workspace,
+                 size_t workspace_bytes, void *stream) {
+  using namespace wt;
+  int st = check_common("ln_linear", dtype, rows, out_features, in_features);
+  if (st != WT_OK) return st;
+  WT_REQUIRE(x && gamma && beta && w && b && y, WT_ERR_ARG, "ln_linear: null pointer");
+  WT_ALIGNED(x);
+  WT_ALIGNED(gamma);
+  WT_ALIGNED(beta);
+  WT_ALIGNED(w);
+  WT_ALIGNED(b);
+  WT_ALIGNED(y);
+  const DlPlan p = dl_plan(rows, out_features, in_features, true, dl_sm_count());
+  WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,
+             "ln_linear: needs a workspace of %zu bytes (given %zu)", p.bytes, workspace ? workspace_bytes : 0);
+  WT_ALIGNED(workspace);
+  void *xn = static_cast<char *>(workspace) + p.xn_off;
+  if (dtype == WT_F16)
+    st = launch_ln<__half>(const_cast<__half *>(static_cast<const __half *>(x)), static_cast<const __half *>(gamma),
+                           static_cast<const __half *>(beta), nullptr, static_cast<__half *>(xn), rows, in_features,
+                           eps, stream);
+  else
+    st = launch_ln<__nv_bfloat16>(const_cast<__nv_bfloat16 *>(static_cast<const __nv_bfloat16 *>(x)),
+                                  static_cast<const __nv_bfloat16 *>(gamma), static_cast<const __nv_bfloat16 *>(beta),
+                                  nullptr, static_cast<__nv_bfloat16 *>(xn), rows, in_features, eps, stream);
+  if (st != WT_OK) return st;
+  return run_gemm(dtype, gelu ? kDlGelu : kDlBias, xn, w, b, nullptr, y, rows, out_features, in_features, p, workspace,
+                  stream);
+}
+
+int wt_linear_residual(int dtype, const void *x, const void *w, const void *b, const void *res, void *y, int rows,
+                       int out_features, int in_features, void *workspace, size_t workspace_bytes, void *stream) {
+  using namespace wt;
+  int st = check_common("linear_residual", dtype, rows, out_features, in_features);
+  if (st != WT_OK) return st;
+  WT_REQUIRE(x && w && b && res && y, WT_ERR_ARG, "linear_residual: null pointer");
+  WT_ALIGNED(x);
+  WT_ALIGNED(w);
+  WT_ALIGNED(b);
+  WT_ALIGNED(res);
+  WT_ALIGNED(y);
+  const DlPlan p = dl_plan(rows, out_features, in_features, false, dl_sm_count());
+  WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,
+             "linear_residual: needs a workspace of %zu bytes (given %zu)", p.bytes,
+             workspace ? workspace_bytes : 0);
+  WT_ALIGNED(workspace);
+  return run_gemm(dtype, kDlResidual, x, w, b, res, y, rows, out_features, in_features, p, workspace, stream);
+}
+
+}  // extern "C"

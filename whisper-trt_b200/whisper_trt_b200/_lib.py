@@ -12,7 +12,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libwhisper_attn_b200.so"
 
-c_int, c_size, c_void = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p
+c_int, c_size, c_void, c_float = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float
 c_char_p = ctypes.c_char_p
 
 # name -> (restype, argtypes); the order of the header
@@ -44,6 +44,10 @@ SIGNATURES = {
     "wt_logits32": (c_int, [c_int, c_void, c_void, c_void, c_int, c_int, c_int, c_void, c_void]),
     "wt_beam_scores_workspace": (c_size, [c_int, c_int]),
     "wt_beam_scores": (c_int, [c_void] * 11 + [c_int] * 9 + [c_void, c_size, c_void]),
+    "wt_dec_linear_workspace": (c_size, [c_int, c_int, c_int, c_int]),
+    "wt_layer_norm_bias": (c_int, [c_int, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_float, c_void]),
+    "wt_ln_linear": (c_int, [c_int] + [c_void] * 6 + [c_int] * 4 + [c_float, c_void, c_size, c_void]),
+    "wt_linear_residual": (c_int, [c_int] + [c_void] * 5 + [c_int] * 3 + [c_void, c_size, c_void]),
 }
 
 # status codes (whisper_attn_b200.h)

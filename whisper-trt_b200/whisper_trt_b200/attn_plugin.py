@@ -79,11 +79,12 @@ def _workspace(dev: torch.device, kind: str, shape: tuple, nbytes: int) -> torch
 
 
 def workspace_errors() -> int:
-    """The device error words of this process's cross-attention workspaces, OR-ed (0: no kernel gave up a wait).
+    """The device error words of this process's cross-attention, logits and decoder-linear workspaces, OR-ed (0: no
+    kernel gave up a wait).
     Reads device memory: synchronises."""
     err = 0
     for (dev, kind, shape), ws in _workspaces.items():
-        if kind in ("cross", "logits"):
+        if kind in ("cross", "logits", "dec_linear"):
             err |= int(ws[:4].view(torch.int32).item())
     return err
 
