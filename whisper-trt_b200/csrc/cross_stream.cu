@@ -119,15 +119,15 @@ __device__ __forceinline__ void store_partial(State<NT> &st, const StreamArgs &a
     }
 }
 
-// The warp's block count for unit u added to the unit's counter, after a warp barrier and a release fence that order
-// the partial this warp stored before it. Returns, in lane 0, whether this warp completed the unit.
+// The warp's block count for unit u added to the unit's counter by one acquire-release atomic (lane 0, after a warp
+// barrier): its release side orders the partial every lane of this warp stored before it, its acquire side the
+// other warps' partials before whatever this warp reads next (combine_unit). Returns, in lane 0, whether this warp
+// completed the unit.
 __device__ __forceinline__ bool publish(const StreamArgs &a, long long u, int nblk, int lane) {
   __syncwarp();
   int old = 0;
-  if (lane == 0) {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a.counters + u), "r"(nblk) : "memory");
-  }
+  if (lane == 0)
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a.counters + u), "r"(nblk) : "memory");
   return old + nblk == a.bpu;
 }
 
@@ -167,8 +167,7 @@ __device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a
 constexpr int kCombineSlots = 4;
 template <typename T, int NT>
 __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
-  __syncwarp();
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  __syncwarp();  // (after lane 0's acquire-release count: every lane's loads below are ordered after it)
   const long long fw = first_warp(u, a.bpu, a.per_warp);
   const int nslots = static_cast<int>(last_warp(u, a.bpu, a.per_warp) - fw + 1);
   const int wh = static_cast<int>(u / a.QG), qg = static_cast<int>(u % a.QG);
@@ -254,9 +253,9 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
 }
 
 // The CTA's service warp: lane i waits for streaming warp i's request (its first unit's partial stored, or none),
-// then adds the warp's block count to the unit's counter behind a GPU-scope fence -- the fence covers the streaming
-// warp's stores, ordered before its mbarrier arrival, which this lane's wait acquires. Units it completes it
-// combines itself. The polls are bounded: on a timeout the error word gets a code and the warp returns.
+// then adds the warp's block count to the unit's counter with an acquire-release atomic -- its release side covers
+// the streaming warp's stores, ordered before its mbarrier arrival, which this lane's wait acquires. Units it
+// completes it combines itself. The polls are bounded: on a timeout the error word gets a code and the warp returns.
 template <typename T, int NT, int kStreamWarps>
 __device__ void serve_requests(const StreamArgs &a, uint64_t *req_bar, const long long *req_u, const int *req_n,
                                int lane) {
@@ -270,8 +269,7 @@ __device__ void serve_requests(const StreamArgs &a, uint64_t *req_bar, const lon
       if (u >= 0) {
         const int nb = req_n[lane];
         int old = 0;
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a.counters + u), "r"(nb) : "memory");
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(a.counters + u), "r"(nb) : "memory");
         completed = old + nb == a.bpu;
       }
     }
