@@ -163,3 +163,44 @@ def test_install_routes_a_module():
     assert mod.self_attn_step_triton is attn_plugin.self_attn_step_triton
     assert mod.self_attn_triton is attn_plugin.self_attn_triton
     assert mod.cross_attn_combine_triton is attn_plugin.cross_attn_combine_triton
+
+
+def test_decoder_linear_arguments_without_a_gpu():
+    """The fused decoder linear layers refuse bad sizes, alignments and workspaces with a status and a message before
+    any device access."""
+    lib = _lib.load()
+    p, keep = _fake(1 << 16)
+    assert lib.wt_dec_linear_workspace(160, 1280, 1280, 0) == 256  # (the device error word)
+    assert lib.wt_dec_linear_workspace(160, 1280, 1280, 1) == 256 + 160 * 1280 * 2  # (+ the normalized rows)
+    assert lib.wt_dec_linear_workspace(0, 1280, 1280, 1) == 0
+    st = lib.wt_ln_linear(0, p, p, p, p, p, p, 5, 128, 60, 0, 1e-5, p, 1 << 16, None)
+    assert st == _lib.WT_ERR_UNSUPPORTED and b"multiple of 8" in lib.wt_last_error()
+    st = lib.wt_ln_linear(0, p, p, p, p, p, None, 5, 128, 64, 0, 1e-5, p, 1 << 16, None)
+    assert st == _lib.WT_ERR_ARG and b"null" in lib.wt_last_error()
+    st = lib.wt_ln_linear(0, p, p, p, p, p, p, 5, 128, 64, 0, 1e-5, p, 16, None)
+    assert st == _lib.WT_ERR_WORKSPACE
+    st = lib.wt_linear_residual(2, p, p, p, p, p, 5, 128, 64, p, 1 << 16, None)
+    assert st == _lib.WT_ERR_DTYPE
+    st = lib.wt_linear_residual(0, p + 4, p, p, p, p, 5, 128, 64, p, 1 << 16, None)
+    assert st == _lib.WT_ERR_ALIGN and b"x" in lib.wt_last_error()
+    st = lib.wt_layer_norm_bias(0, p, p, p, p, p, 0, 64, 1e-5, None)
+    assert st == _lib.WT_ERR_ARG
+    st = lib.wt_layer_norm_bias(0, p, p, p, p, p, 4, 60, 1e-5, None)
+    assert st == _lib.WT_ERR_UNSUPPORTED
+
+
+def test_decoder_linear_python_checks():
+    from whisper_trt_b200 import decoder_kernels as dk
+
+    x = torch.zeros(5, 64, dtype=torch.half)
+    w = torch.zeros(128, 64, dtype=torch.half)
+    b = torch.zeros(128, dtype=torch.half)
+    with pytest.raises(ValueError, match="CUDA"):
+        dk.linear_residual(x, w, b, torch.zeros(5, 128, dtype=torch.half))
+    with pytest.raises(ValueError, match="do not match"):
+        dk.ln_linear(x, torch.zeros(64, dtype=torch.half), torch.zeros(64, dtype=torch.half), w[:, :32], b)
+    with pytest.raises(TypeError, match="one dtype"):
+        dk.linear_residual(x, w.float(), b, torch.zeros(5, 128, dtype=torch.half))
+    with pytest.raises(ValueError, match="gamma"):
+        dk.layer_norm_bias(x, torch.zeros(32, dtype=torch.half), torch.zeros(64, dtype=torch.half),
+                           torch.zeros(64, dtype=torch.half))
