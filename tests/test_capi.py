@@ -204,3 +204,15 @@ def test_decoder_linear_python_checks():
     with pytest.raises(ValueError, match="gamma"):
         dk.layer_norm_bias(x, torch.zeros(32, dtype=torch.half), torch.zeros(64, dtype=torch.half),
                            torch.zeros(64, dtype=torch.half))
+
+
+def test_triton_baseline_without_the_reference(tmp_path):
+    """The GPU baseline module reports, and does not fail, when no reference package is staged."""
+    import json
+    import subprocess
+    import sys
+
+    root = Path(__file__).resolve().parent.parent
+    out = subprocess.run([sys.executable, "-m", "whisper_trt_b200.triton_baseline", "--ref", str(tmp_path)],
+                         cwd=root / "whisper-trt_b200", capture_output=True, text=True, timeout=300, check=True)
+    assert "unavailable" in json.loads(out.stdout.strip().splitlines()[-1])
