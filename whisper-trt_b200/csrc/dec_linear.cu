@@ -23,6 +23,7 @@
 //   * every mbarrier wait is bounded (a timeout records an error in the workspace's device word and the kernel goes
 //     on, then frees its tensor memory).
 #include <cstdlib>
+#include <mutex>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -51,11 +52,13 @@ struct DlArgs {
   const void *bias;  // [V]
   const void *res;   // [N, V] (residual mode)
   void *y;           // [N, V]
-  int N, V, kblocks, splits, kb_per, vtiles, nmma, tcols, stages, ring_bytes;
+  int N, V, kblocks, splits, kb_per, vtiles, nmma, tcols, stages, ring_bytes, res_bytes;
 };
 
+// nmma: the rows of a unit (a row chunk; the MMA's N, a multiple of 16). res_bytes: a region after the ring that
+// receives this CTA's share of the residual rows while the MMAs run (residual mode with k splits).
 struct DlPlan {
-  int chunks, vtiles, kblocks, splits, kb_per, nmma, tcols, stages, stage_bytes, ring_bytes, smem, grid;
+  int chunks, vtiles, kblocks, splits, kb_per, nmma, tcols, stages, stage_bytes, ring_bytes, res_bytes, smem, grid;
   size_t xn_off, bytes;
 };
 
@@ -70,30 +73,51 @@ int max_splits() {
   return v;
 }
 
-DlPlan dl_plan(int N, int V, int K, bool ln, int sms) {
+// Row chunks per 256 rows forced by WT_DL_CHUNKS (a tuning knob, 1-4), else 0 (chosen by the cost model).
+int row_chunks() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("WT_DL_CHUNKS");
+    const int x = e ? atoi(e) : 0;
+    v = (x >= 1 && x <= 4) ? x : 0;
+  }
+  return v;
+}
+
+int min_chunks(int N) { return (N + kDlMaxRows - 1) / kDlMaxRows; }
+int chunk_rows(int N, int c) { return ((N + c - 1) / c + 15) / 16 * 16; }  // rows per chunk (<= 256)
+
+// `ln`: the plan of ln_linear (a workspace for the normalized rows), else of linear_residual. `c`: row chunks (0:
+// the fewest, ceil(N / 256)); at most `smax` k splits.
+DlPlan dl_plan(int N, int V, int K, bool ln, int sms, int c = 0, int smax = kDlMaxSplits) {
   DlPlan p{};
-  p.chunks = (N + kDlMaxRows - 1) / kDlMaxRows;
+  if (c < min_chunks(N)) c = min_chunks(N);
+  const int rc = chunk_rows(N, c);
+  p.chunks = (N + rc - 1) / rc;
   p.vtiles = (V + kDlTileV - 1) / kDlTileV;
   p.kblocks = (K + kDlKBlock - 1) / kDlKBlock;
   const int tiles = p.chunks * p.vtiles;
   int s = sms / tiles;  // splits: enough CTAs for the SMs, at most a cluster, at least 2 k blocks each
   if (s > kDlMaxSplits) s = kDlMaxSplits;
   if (s > max_splits()) s = max_splits();
+  if (s > smax) s = smax;
   if (s > p.kblocks / 2) s = p.kblocks / 2;
   if (s < 1) s = 1;
   p.kb_per = (p.kblocks + s - 1) / s;
   p.splits = (p.kblocks + p.kb_per - 1) / p.kb_per;  // (no empty split)
-  const int nrows = N < kDlMaxRows ? N : kDlMaxRows;
-  p.nmma = (nrows + 15) / 16 * 16;
+  p.nmma = rc;
   p.tcols = 32;
   while (p.tcols < p.nmma) p.tcols <<= 1;
   p.stage_bytes = kDlTileV * 128 + (p.nmma * 128 + 1023) / 1024 * 1024;
-  const int cap = (200 * 1024) / p.stage_bytes < 8 ? (200 * 1024) / p.stage_bytes : 8;
+  // residual mode with k splits: this CTA's share of the rows (at most ceil(nmma / splits)) x 128 features
+  p.res_bytes = (!ln && p.splits > 1) ? ((p.nmma + p.splits - 1) / p.splits) * kDlTileV * 2 : 0;
+  const int budget = 200 * 1024 - p.res_bytes;
+  const int cap = budget / p.stage_bytes < 8 ? budget / p.stage_bytes : 8;
   p.stages = p.kb_per < cap ? p.kb_per : cap;
   p.ring_bytes = p.stages * p.stage_bytes;
   const int part_bytes = p.splits > 1 ? p.nmma * kDlTileV * 4 : 0;  // the partial, parked over the idle ring
   if (p.ring_bytes < part_bytes) p.ring_bytes = part_bytes;
-  p.smem = 1024 + p.ring_bytes + (2 * p.stages + 2) * 8 + 16;
+  p.smem = 1024 + p.ring_bytes + p.res_bytes + (2 * p.stages + 2) * 8 + 16;
   p.grid = tiles * p.splits;
   p.xn_off = 256;  // [0, 256): the device error word
   p.bytes = p.xn_off + (ln ? (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256 : 0);
@@ -119,6 +143,73 @@ __device__ __forceinline__ float ld_f(const void *p, size_t i) {
   return Elem<T>::to_float(static_cast<const T *>(p)[i]);
 }
 
+__device__ __forceinline__ void dl_cp16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void dl_cp_commit_wait() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Four consecutive 16-bit values <-> floats (8 bytes, 8-byte aligned).
+template <typename T>
+__device__ __forceinline__ void unpack4(uint2 u, float (&f)[4]) {
+  const T *h = reinterpret_cast<const T *>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) f[e] = Elem<T>::to_float(h[e]);
+}
+template <typename T>
+__device__ __forceinline__ uint2 pack4(const T (&h)[4]) {
+  uint2 u;
+  T *o = reinterpret_cast<T *>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) o[e] = h[e];
+  return u;
+}
+
+// One CTA's share of a tile's rows, rows [r0, r1) of the unit: the sum of the cluster's S partials (read from the
+// CTAs' shared memory, 16 bytes at a time, in split order: the same sums whichever CTA finished first), then the
+// fused epilogue. Thread et (0-127) takes features 4 (et % 32) .. + 3 of rows r0 + et / 32 + 4 i; kR rows per batch
+// keep ~32 partial loads in flight. The residual share is already in shared memory (`rsm`, [row - r0][128]).
+template <typename T, int MODE, int S>
+__device__ __forceinline__ void reduce_share(const DlArgs &a, const float4 *const (&peer)[kDlMaxSplits],
+                                             const T *rsm, const float (&bv4)[4], int et, int n0, int r0, int r1,
+                                             int v0) {
+  constexpr int kR = 32 / S;
+  const int f4 = et & 31, rsub = et >> 5;
+  const int vv = v0 + 4 * f4;
+  T *y = static_cast<T *>(a.y);
+  for (int n = r0 + rsub; n < r1; n += 4 * kR) {
+    float4 val[kR][S];
+#pragma unroll
+    for (int q = 0; q < kR; ++q) {
+      const int row = n + 4 * q;
+#pragma unroll
+      for (int s2 = 0; s2 < S; ++s2)
+        val[q][s2] = row < r1 ? peer[s2][row * (kDlTileV / 4) + f4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < kR; ++q) {
+      const int row = n + 4 * q;
+      if (row >= r1 || vv >= a.V) continue;  // (V % 8 == 0: the 4 features are all in or all out)
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s2 = 0; s2 < S; ++s2) {
+        acc[0] += val[q][s2].x;
+        acc[1] += val[q][s2].y;
+        acc[2] += val[q][s2].z;
+        acc[3] += val[q][s2].w;
+      }
+      float rr[4] = {0.f, 0.f, 0.f, 0.f};
+      if (MODE == kDlResidual)
+        unpack4<T>(*reinterpret_cast<const uint2 *>(rsm + (row - r0) * kDlTileV + 4 * f4), rr);
+      T o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = dl_out<T, MODE>(acc[e], bv4[e], rr[e]);
+      *reinterpret_cast<uint2 *>(y + static_cast<size_t>(n0 + row) * a.V + vv) = pack4<T>(o);
+    }
+  }
+}
+
 // One unit per CTA: blockIdx.x = tile * splits + split; the splits of a tile are one cluster (rank = split).
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kDlThreads)
@@ -132,14 +223,16 @@ __global__ void __launch_bounds__(kDlThreads)
   const int a_bytes = kDlTileV * 128, b_bytes = a.nmma * 128;
   const int stage_bytes = a_bytes + ((b_bytes + 1023) & ~1023);
   const int stages = a.stages;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.ring_bytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.ring_bytes + a.res_bytes);
   uint64_t *empty = full + stages;
   uint64_t *acc_full = empty + stages;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = a.splits, sp = static_cast<int>(blockIdx.x) % S, t = static_cast<int>(blockIdx.x) / S;
-  const int v0 = (t % a.vtiles) * kDlTileV, n0 = (t / a.vtiles) * kDlMaxRows;
-  const int nn = min(kDlMaxRows, a.N - n0);
+  const int v0 = (t % a.vtiles) * kDlTileV, n0 = (t / a.vtiles) * a.nmma;
+  const int nn = min(a.nmma, a.N - n0);
+  const int rpc = (nn + S - 1) / S, r0 = sp * rpc, r1 = min(nn, r0 + rpc);  // this CTA's rows of the reduction
+  float bv4[4] = {0.f, 0.f, 0.f, 0.f};  // (k splits: the bias of the features an epilogue thread reduces)
   const int kb0 = sp * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per), nkb = kb1 - kb0;
 
   if (warp == 0) {
@@ -214,86 +307,88 @@ __global__ void __launch_bounds__(kDlThreads)
   } else {  // epilogue warps: lane quarter warp % 4 = features v0 + 32 (warp % 4) + lane
     pdl_wait();
     pdl_launch_dependents();
-    const int quarter = warp & 3;
+    const int quarter = warp & 3, et = tid - 64;
     const int v = v0 + quarter * 32 + lane;
     const float bv = (S == 1 && v < a.V) ? ld_f<T>(a.bias, v) : 0.f;
+    if (S > 1) {
+      // while the MMAs run: the bias of this thread's reduction features and, in residual mode, this CTA's share of
+      // the residual rows into shared memory (16-byte copies; out-of-range features are not needed)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int vv = v0 + 4 * (et & 31) + e;
+        bv4[e] = vv < a.V ? ld_f<T>(a.bias, vv) : 0.f;
+      }
+      if (MODE == kDlResidual) {
+        unsigned char *rsm = smem + a.ring_bytes;
+        for (int c = et; c < (r1 - r0) * (kDlTileV / 8); c += 32 * kDlEpiWarps) {
+          const int row = r0 + c / (kDlTileV / 8), col = v0 + (c % (kDlTileV / 8)) * 8;
+          if (col < a.V) dl_cp16(rsm + c * 16, static_cast<const T *>(a.res) + static_cast<size_t>(n0 + row) * a.V + col);
+        }
+      }
+    }
     mbar_wait_bounded(&acc_full[0], 0, a.err, kDlErrTimeout);
     tc_fence_after();
     const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     T *y = static_cast<T *>(a.y);
     float *part = reinterpret_cast<float *>(smem);  // [row][128 features], over the idle ring
-    for (int c0 = 0; c0 < a.nmma; c0 += 16) {
-      uint32_t r[16];
-      tmem_ld16(base + static_cast<uint32_t>(c0), r);
-      tmem_wait_ld();
+    for (int c0 = 0; c0 < a.nmma; c0 += 64) {  // 64 accumulator columns (rows) per tensor-memory wait
+      uint32_t r[4][16];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int n = c0 + q;
-        if (n < nn) {
-          if (S == 1) {
-            if (v < a.V) {
-              const size_t o = static_cast<size_t>(n0 + n) * a.V + v;
-              y[o] = dl_out<T, MODE>(__uint_as_float(r[q]), bv, MODE == kDlResidual ? ld_f<T>(a.res, o) : 0.f);
-            }
-          } else {
-            part[n * kDlTileV + quarter * 32 + lane] = __uint_as_float(r[q]);
+      for (int j = 0; j < 4; ++j)
+        if (c0 + 16 * j < a.nmma) tmem_ld16(base + static_cast<uint32_t>(c0 + 16 * j), r[j]);
+      tmem_wait_ld();
+      if (S == 1) {
+        float rs[4][16];  // (every residual of the batch loaded before its stores: y may be the residual itself)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int n = c0 + 16 * j + q;
+            rs[j][q] = (MODE == kDlResidual && n < nn && v < a.V) ? ld_f<T>(a.res, static_cast<size_t>(n0 + n) * a.V + v)
+                                                                  : 0.f;
           }
-        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int n = c0 + 16 * j + q;
+            if (n < nn && v < a.V)
+              y[static_cast<size_t>(n0 + n) * a.V + v] = dl_out<T, MODE>(__uint_as_float(r[j][q]), bv, rs[j][q]);
+          }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int n = c0 + 16 * j + q;
+            if (n < nn) part[n * kDlTileV + quarter * 32 + lane] = __uint_as_float(r[j][q]);
+          }
       }
     }
+    if (S > 1 && MODE == kDlResidual) dl_cp_commit_wait();
     tc_fence_before();
   }
   if (S > 1) {
-    // This CTA's share of the tile's rows: the sum of the splits' partials (read from their CTAs' shared memory,
-    // 16 bytes at a time, every split's value of a batch of rows in flight) in split order, then the epilogue.
+    // This CTA's share of the tile's rows: the sum of the splits' partials through distributed shared memory, then
+    // the epilogue (reduce_share).
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();  // every split's partial is in its CTA's shared memory
+    cluster.sync();  // every split's partial is in its CTA's shared memory (and the residual share in this one's)
     if (warp >= 2) {
-      const int f4 = (tid - 64) & 31, rsub = (tid - 64) >> 5;  // features 4 f4 .. 4 f4 + 3; rows r0 + rsub + 4 i
-      const int rpc = (nn + S - 1) / S, r0 = sp * rpc, r1 = min(nn, r0 + rpc);
       const float *part = reinterpret_cast<const float *>(smem);
       const float4 *peer[kDlMaxSplits];
 #pragma unroll
       for (int s2 = 0; s2 < kDlMaxSplits; ++s2)
         peer[s2] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(part, s2 < S ? s2 : 0));
-      float bv4[4], rs[4][4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) bv4[e] = v0 + 4 * f4 + e < a.V ? ld_f<T>(a.bias, v0 + 4 * f4 + e) : 0.f;
-      T *y = static_cast<T *>(a.y);
-      constexpr int kR = 4;  // rows per thread per batch
-      for (int n = r0 + rsub; n < r1; n += 4 * kR) {
-        float4 val[kR][kDlMaxSplits];
-#pragma unroll
-        for (int q = 0; q < kR; ++q) {
-          const int row = n + 4 * q;
-#pragma unroll
-          for (int s2 = 0; s2 < kDlMaxSplits; ++s2)
-            val[q][s2] = (s2 < S && row < r1) ? peer[s2][row * (kDlTileV / 4) + f4] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int vv = v0 + 4 * f4 + e;
-            rs[q][e] = (MODE == kDlResidual && row < r1 && vv < a.V)
-                           ? ld_f<T>(a.res, static_cast<size_t>(n0 + row) * a.V + vv) : 0.f;
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < kR; ++q) {
-          const int row = n + 4 * q;
-          if (row >= r1) continue;
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int s2 = 0; s2 < kDlMaxSplits; ++s2) {  // in split order (absent splits add +0)
-            acc[0] += val[q][s2].x;
-            acc[1] += val[q][s2].y;
-            acc[2] += val[q][s2].z;
-            acc[3] += val[q][s2].w;
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int vv = v0 + 4 * f4 + e;
-            if (vv < a.V) y[static_cast<size_t>(n0 + row) * a.V + vv] = dl_out<T, MODE>(acc[e], bv4[e], rs[q][e]);
-          }
-        }
+      const T *rsm = reinterpret_cast<const T *>(smem + a.ring_bytes);
+      const int et = tid - 64;
+      switch (S) {
+        case 2: reduce_share<T, MODE, 2>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
+        case 3: reduce_share<T, MODE, 3>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
+        case 4: reduce_share<T, MODE, 4>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
+        case 5: reduce_share<T, MODE, 5>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
+        case 6: reduce_share<T, MODE, 6>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
+        case 7: reduce_share<T, MODE, 7>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
+        default: reduce_share<T, MODE, 8>(a, peer, rsm, bv4, et, n0, r0, r1, v0); break;
       }
     }
     cluster.sync();  // (no CTA leaves while another may still read its shared memory)
@@ -435,14 +530,107 @@ int dl_sm_count() {
   return g_dl_sm[dev];
 }
 
-template <typename T, int MODE>
-int launch_gemm(const DlPlan &p, const CUtensorMap &wm, const CUtensorMap &xm, const DlArgs &a, void *stream) {
-  auto kernel = dec_gemm_kernel<T, MODE>;
-  static int attr = 0;
-  if (p.smem > attr) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
-    attr = p.smem;
+// Thread-block clusters of `splits` CTAs of `kernel` (with `smem` bytes each) resident at once on this device --
+// the clusters of one launch must fit in one wave. Cached per (kernel, device, splits, smem).
+template <typename Kern>
+int max_clusters(Kern kernel, int splits, int smem) {
+  struct Entry {
+    const void *k;
+    int dev, splits, smem, n;
+  };
+  static Entry cache[128];
+  static int used = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void *kp = reinterpret_cast<const void *>(kernel);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].k == kp && cache[i].dev == dev && cache[i].splits == splits && cache[i].smem == smem)
+        return cache[i].n;
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(splits));
+  cfg.blockDim = dim3(kDlThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = static_cast<unsigned>(splits);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = dl_sm_count() / splits;  // (the query failed: assume every SM holds one CTA)
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (used < 128) cache[used++] = Entry{kp, dev, splits, smem, n};
+  return n;
+}
+
+// Estimated duration (us) of a plan, from measurements of this kernel on B200 at decode sizes: a CTA streams its
+// stages at ~75 GB/s, and parking plus reducing its fp32 partial moves ~38 GB/s; launches of more CTAs than fit run
+// in waves.
+double plan_cost(const DlPlan &p, int sms) {
+  const double stream = static_cast<double>(p.kb_per) * (kDlTileV * 128.0 + p.nmma * 128.0) / 75e3;
+  const double reduce = p.splits > 1 ? p.nmma * 512.0 / 38e3 : 0.0;
+  const int waves = p.splits > 1 ? 1 : (p.grid + sms - 1) / sms;
+  return waves * (stream + reduce);
+}
+
+// The plan to launch: for each candidate row chunking (the fewest chunks, and more while a chunk keeps >= 64
+// rows), the most k splits whose clusters all fit in one wave, costed by plan_cost; the cheapest wins (ties: fewer
+// chunks).
+template <typename Kern>
+DlPlan tuned_plan(Kern kernel, int N, int V, int K, bool ln) {
+  const int sms = dl_sm_count(), c0 = min_chunks(N);
+  DlPlan best{};
+  double best_t = 0.0;
+  bool have = false;
+  for (int c = c0; c <= 4 * c0; ++c) {
+    if (row_chunks() != 0 && c != c0 * row_chunks()) continue;
+    if (row_chunks() == 0 && c > c0 && chunk_rows(N, c) < 64) break;
+    if (row_chunks() == 0 && c > c0 && chunk_rows(N, c) == chunk_rows(N, c - 1)) continue;
+    int smax = kDlMaxSplits;
+    DlPlan p = dl_plan(N, V, K, ln, sms, c, smax);
+    while (p.splits > 1 && p.chunks * p.vtiles > max_clusters(kernel, p.splits, p.smem)) {
+      smax = p.splits - 1;
+      p = dl_plan(N, V, K, ln, sms, c, smax);
+    }
+    const double t = plan_cost(p, sms);
+    if (!have || t < best_t - 1e-9) {
+      best = p;
+      best_t = t;
+      have = true;
+    }
+  }
+  return have ? best : dl_plan(N, V, K, ln, sms, c0);
+}
+
+// The GEMM with its fused epilogue; `x` its rows (for ln_linear the normalized rows in the workspace).
+template <typename T, int MODE>
+int launch_gemm(int dtype, const void *x, const void *w, const void *b, const void *res, void *y, int N, int V, int K,
+                bool ln, void *workspace, void *stream) {
+  auto kernel = dec_gemm_kernel<T, MODE>;
+  static bool smem_set[64] = {};  // (per instantiation: the largest dynamic shared memory, once per device; every
+  int dev = 0;                    // plan stays below it, and the cluster-occupancy query needs it set)
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !smem_set[dev]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    smem_set[dev] = true;
+  }
+  const DlPlan p = tuned_plan(kernel, N, V, K, ln);
+  CUtensorMap wm, xm;
+  int st = encode_tile_map(&wm, w, static_cast<unsigned long long>(V), static_cast<unsigned long long>(K), kDlTileV,
+                           dtype);
+  if (st != WT_OK) return st;
+  st = encode_tile_map(&xm, x, static_cast<unsigned long long>(N), static_cast<unsigned long long>(K), p.nmma, dtype);
+  if (st != WT_OK) return st;
+  DlArgs a{reinterpret_cast<int *>(workspace), b, res, y, N, V, p.kblocks, p.splits, p.kb_per, p.vtiles, p.nmma,
+           p.tcols, p.stages, p.ring_bytes, p.res_bytes};
   return launch_clustered("dec_linear", kernel, dim3(p.grid), dim3(kDlThreads), p.smem, stream, p.splits, wm, xm, a);
 }
 
@@ -461,26 +649,19 @@ int check_common(const char *what, int dtype, int N, int V, int K) {
   return WT_OK;
 }
 
-// The GEMM with its fused epilogue; `x` its rows (for ln_linear the normalized rows in the workspace).
 int run_gemm(int dtype, int mode, const void *x, const void *w, const void *b, const void *res, void *y, int N,
-             int V, int K, const DlPlan &p, void *workspace, void *stream) {
-  CUtensorMap wm, xm;
-  int st = encode_tile_map(&wm, w, static_cast<unsigned long long>(V), static_cast<unsigned long long>(K), kDlTileV,
-                           dtype);
-  if (st != WT_OK) return st;
-  st = encode_tile_map(&xm, x, static_cast<unsigned long long>(N), static_cast<unsigned long long>(K), p.nmma, dtype);
-  if (st != WT_OK) return st;
-  DlArgs a{reinterpret_cast<int *>(workspace), b, res, y, N, V, p.kblocks, p.splits, p.kb_per, p.vtiles, p.nmma,
-           p.tcols, p.stages, p.ring_bytes};
+             int V, int K, bool ln, void *workspace, void *stream) {
   const bool bf = dtype == WT_BF16;
   switch (mode) {
     case kDlGelu:
-      return bf ? launch_gemm<__nv_bfloat16, kDlGelu>(p, wm, xm, a, stream) : launch_gemm<__half, kDlGelu>(p, wm, xm, a, stream);
+      return bf ? launch_gemm<__nv_bfloat16, kDlGelu>(dtype, x, w, b, res, y, N, V, K, ln, workspace, stream)
+                : launch_gemm<__half, kDlGelu>(dtype, x, w, b, res, y, N, V, K, ln, workspace, stream);
     case kDlResidual:
-      return bf ? launch_gemm<__nv_bfloat16, kDlResidual>(p, wm, xm, a, stream)
-                : launch_gemm<__half, kDlResidual>(p, wm, xm, a, stream);
+      return bf ? launch_gemm<__nv_bfloat16, kDlResidual>(dtype, x, w, b, res, y, N, V, K, ln, workspace, stream)
+                : launch_gemm<__half, kDlResidual>(dtype, x, w, b, res, y, N, V, K, ln, workspace, stream);
     default:
-      return bf ? launch_gemm<__nv_bfloat16, kDlBias>(p, wm, xm, a, stream) : launch_gemm<__half, kDlBias>(p, wm, xm, a, stream);
+      return bf ? launch_gemm<__nv_bfloat16, kDlBias>(dtype, x, w, b, res, y, N, V, K, ln, workspace, stream)
+                : launch_gemm<__half, kDlBias>(dtype, x, w, b, res, y, N, V, K, ln, workspace, stream);
   }
 }
 
@@ -543,8 +724,8 @@ int wt_ln_linear(int dtype, const void *x, const void *gamma, const void *beta, 
                                   static_cast<const __nv_bfloat16 *>(gamma), static_cast<const __nv_bfloat16 *>(beta),
                                   nullptr, static_cast<__nv_bfloat16 *>(xn), rows, in_features, eps, stream);
   if (st != WT_OK) return st;
-  return run_gemm(dtype, gelu ? kDlGelu : kDlBias, xn, w, b, nullptr, y, rows, out_features, in_features, p, workspace,
-                  stream);
+  return run_gemm(dtype, gelu ? kDlGelu : kDlBias, xn, w, b, nullptr, y, rows, out_features, in_features, true,
+                  workspace, stream);
 }
 
 int wt_linear_residual(int dtype, const void *x, const void *w, const void *b, const void *res, void *y, int rows,
@@ -563,7 +744,7 @@ int wt_linear_residual(int dtype, const void *x, const void *w, const void *b, c
              "linear_residual: needs a workspace of %zu bytes (given %zu)", p.bytes,
              workspace ? workspace_bytes : 0);
   WT_ALIGNED(workspace);
-  return run_gemm(dtype, kDlResidual, x, w, b, res, y, rows, out_features, in_features, p, workspace, stream);
+  return run_gemm(dtype, kDlResidual, x, w, b, res, y, rows, out_features, in_features, false, workspace, stream);
 }
 
 }  // extern "C"
