@@ -17,11 +17,19 @@
 //     a cluster barrier each CTA sums its share of the tile's rows over all the cluster's partials through
 //     distributed shared memory, in split order (the same sums whichever CTA finishes first), and applies the
 //     fused epilogue -- no partial leaves the chip;
+//   * the plan: the most splits whose clusters are all resident at once (cudaOccupancyMaxActiveClusters: a cluster
+//     of 7 needs 7 SMs of one GPC, so 20 such clusters would run in two waves), and the rows cut into chunks of
+//     >= 64 when a cost model fitted to this kernel's measured rates on B200 (a CTA streams its stages at ~75 GB/s;
+//     parking and reducing its partial moves ~38 GB/s) says that smaller partials pay for re-reading the weights;
+//   * while the MMAs run, the epilogue threads fetch the bias and (residual mode) their CTA's share of the residual
+//     rows into shared memory; the accumulator leaves tensor memory 64 columns per wait; the reduction keeps ~32
+//     partial loads in flight per thread whatever the split count;
 //   * ln_linear first normalizes the rows into the workspace with a row kernel; the GEMM is launched after it with
 //     programmatic dependent launch and issues its first stages' weight loads before waiting for it (the weights
 //     are not its output), so the weight stream overlaps the LayerNorm;
 //   * every mbarrier wait is bounded (a timeout records an error in the workspace's device word and the kernel goes
 //     on, then frees its tensor memory).
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 
@@ -82,6 +90,16 @@ int row_chunks() {
     v = (x >= 1 && x <= 4) ? x : 0;
   }
   return v;
+}
+
+// WT_DL_TRACE=1: print every plan the chooser weighs to stderr (a tuning aid; off by default).
+bool trace_plans() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("WT_DL_TRACE");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 int min_chunks(int N) { return (N + kDlMaxRows - 1) / kDlMaxRows; }
@@ -597,10 +615,16 @@ DlPlan tuned_plan(Kern kernel, int N, int V, int K, bool ln) {
     int smax = kDlMaxSplits;
     DlPlan p = dl_plan(N, V, K, ln, sms, c, smax);
     while (p.splits > 1 && p.chunks * p.vtiles > max_clusters(kernel, p.splits, p.smem)) {
+      if (trace_plans())
+        fprintf(stderr, "[dec_linear] rows %d out %d in %d, %d chunks of %d: %d clusters of %d do not fit (%d resident)\n",
+                N, V, K, p.chunks, p.nmma, p.chunks * p.vtiles, p.splits, max_clusters(kernel, p.splits, p.smem));
       smax = p.splits - 1;
       p = dl_plan(N, V, K, ln, sms, c, smax);
     }
     const double t = plan_cost(p, sms);
+    if (trace_plans())
+      fprintf(stderr, "[dec_linear] rows %d out %d in %d: %d chunks of %d rows, %d splits of %d k blocks, grid %d, "
+              "cost %.2f us\n", N, V, K, p.chunks, p.nmma, p.splits, p.kb_per, p.grid, t);
     if (!have || t < best_t - 1e-9) {
       best = p;
       best_t = t;
