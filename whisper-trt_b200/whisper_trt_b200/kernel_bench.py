@@ -148,41 +148,47 @@ def self_step(a) -> dict:
 def dec_linear(a) -> dict:
     """The decoder step's six fused linear layers of one layer (whisper-large: d 1280, MLP 5120) at ``rows`` rows:
     qkv = ln_linear(x, 3d), y += out(attn) (linear_residual), q = ln_linear(x, d), y += xout(attn),
-    h = ln_linear(x, 4d, gelu), y += fc2(h) -- each timed alone and the six in sequence; 3 rotating weight copies
-    so the weights stream from HBM. Bytes: weights + biases + the rows read and written."""
+    h = ln_linear(x, 4d, gelu), y += fc2(h) -- each timed alone and the six in sequence. Each op rotates through
+    enough weight copies (>= 256 MB, twice the L2) that its weights stream from HBM, as a decoder step's 32 layers'
+    weights do. Bytes: weights + biases + the rows read and written."""
     from . import _lib
     from . import decoder_kernels as dk
 
     _lib.set_launch_flags(_lib.WT_LAUNCH_PDL)  # (as the decoder step launches them)
     dev, n, d = "cuda", a.rows, a.d_model
     g = torch.Generator(device=dev).manual_seed(0)
-    L = 3
+
     def lin(o, i):
-        return ((torch.randn(L, o, i, generator=g, device=dev) * 0.02).half(),
-                (torch.randn(L, o, generator=g, device=dev) * 0.02).half())
+        copies = max(3, -(-(256 << 20) // (o * i * 2)))  # (the rotation exceeds L2)
+        return ((torch.randn(copies, o, i, generator=g, device=dev) * 0.02).half(),
+                (torch.randn(copies, o, generator=g, device=dev) * 0.02).half())
     W = {"qkv": lin(3 * d, d), "out": lin(d, d), "q": lin(d, d), "xout": lin(d, d), "fc1": lin(4 * d, d),
          "fc2": lin(d, 4 * d)}
-    ln = [((1 + 0.1 * torch.randn(L, d, generator=g, device=dev)).half(),
-           (0.1 * torch.randn(L, d, generator=g, device=dev)).half()) for _ in range(3)]
+    ln = [((1 + 0.1 * torch.randn(3, d, generator=g, device=dev)).half(),
+           (0.1 * torch.randn(3, d, generator=g, device=dev)).half()) for _ in range(3)]
     x = torch.randn(n, d, generator=g, device=dev).half()
     y_attn = torch.randn(n, d, generator=g, device=dev).half()
     qkv = torch.empty(n, 3 * d, device=dev, dtype=torch.float16)
     q = torch.empty(n, d, device=dev, dtype=torch.float16)
     h = torch.empty(n, 4 * d, device=dev, dtype=torch.float16)
     i = [0]
+    def wj(name, j):  # this op's weight copy for call j
+        w, b = W[name]
+        return w[j % w.shape[0]], b[j % w.shape[0]]
+
     ops = {
-        "qkv": lambda j: dk.ln_linear(x, ln[0][0][j], ln[0][1][j], W["qkv"][0][j], W["qkv"][1][j], out=qkv),
-        "out": lambda j: dk.linear_residual(y_attn, W["out"][0][j], W["out"][1][j], x, out=x),
-        "q": lambda j: dk.ln_linear(x, ln[1][0][j], ln[1][1][j], W["q"][0][j], W["q"][1][j], out=q),
-        "xout": lambda j: dk.linear_residual(y_attn, W["xout"][0][j], W["xout"][1][j], x, out=x),
-        "fc1": lambda j: dk.ln_linear(x, ln[2][0][j], ln[2][1][j], W["fc1"][0][j], W["fc1"][1][j], gelu=True, out=h),
-        "fc2": lambda j: dk.linear_residual(h, W["fc2"][0][j], W["fc2"][1][j], x, out=x),
+        "qkv": lambda j: dk.ln_linear(x, ln[0][0][j % 3], ln[0][1][j % 3], *wj("qkv", j), out=qkv),
+        "out": lambda j: dk.linear_residual(y_attn, *wj("out", j), x, out=x),
+        "q": lambda j: dk.ln_linear(x, ln[1][0][j % 3], ln[1][1][j % 3], *wj("q", j), out=q),
+        "xout": lambda j: dk.linear_residual(y_attn, *wj("xout", j), x, out=x),
+        "fc1": lambda j: dk.ln_linear(x, ln[2][0][j % 3], ln[2][1][j % 3], *wj("fc1", j), gelu=True, out=h),
+        "fc2": lambda j: dk.linear_residual(h, *wj("fc2", j), x, out=x),
     }
     res = {"kernel": "dec_linear", "rows": n, "d_model": d}
     total_bytes = 0
     for name, op in ops.items():
         def run(op=op):
-            j = i[0] % L
+            j = i[0]
             i[0] += 1
             op(j)
         sec = _time(run, a.reps)
@@ -191,13 +197,13 @@ def dec_linear(a) -> dict:
         total_bytes += nb
         xin = {"qkv": x, "out": y_attn, "q": x, "xout": y_attn, "fc1": x, "fc2": h}[name]
         def base(name=name, xin=xin):  # cuBLAS through torch: the GEMM + bias alone, no LayerNorm / residual
-            j = i[0] % L
+            w, b = wj(name, i[0])
             i[0] += 1
-            torch.addmm(W[name][1][j], xin, W[name][0][j].t())
+            torch.addmm(b, xin, w.t())
         sec_b = _time(base, a.reps)
         res[name] = {"us": round(sec * 1e6, 2), "gbs": round(nb / sec / 1e9, 1), "torch_addmm_us": round(sec_b * 1e6, 2)}
     def layer():
-        j = i[0] % L
+        j = i[0]
         i[0] += 1
         for op in ops.values():
             op(j)
