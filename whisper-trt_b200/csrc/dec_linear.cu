@@ -639,11 +639,20 @@ template <typename T, int MODE>
 int launch_gemm(int dtype, const void *x, const void *w, const void *b, const void *res, void *y, int N, int V, int K,
                 bool ln, void *workspace, void *stream) {
   auto kernel = dec_gemm_kernel<T, MODE>;
-  static bool smem_set[64] = {};  // (per instantiation: the largest dynamic shared memory, once per device; every
-  int dev = 0;                    // plan stays below it, and the cluster-occupancy query needs it set)
+  // (per instantiation, once per device: the largest dynamic shared memory the device lets a block opt into, less
+  // the kernel's static shared memory; every plan stays below it, and the cluster-occupancy query needs it set)
+  static bool smem_set[64] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !smem_set[dev]) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    int optin = 0;
+    cudaFuncAttributes fa{};
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, kernel) != cudaSuccess ||
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - static_cast<int>(fa.sharedSizeBytes)) != cudaSuccess)
+      return fail(WT_ERR_CUDA, "dec_linear: cannot opt into %d bytes of shared memory: %s", optin,
+                  cudaGetErrorString(cudaGetLastError()));
     smem_set[dev] = true;
   }
   const DlPlan p = tuned_plan(kernel, N, V, K, ln);
