@@ -1,14 +1,14 @@
 """Time one kernel of the package on synthetic inputs (CUDA events on the launching stream, warm) and print one
 JSON line -- the per-kernel numbers beside bench.py's whole-step line, and the commands the ncu summaries use.
 
-    python -m whisper_trt_b200.kernel_bench beam_scores --windows 32 --beams 5 [--timestamps] [--reps 20]
-    python -m whisper_trt_b200.kernel_bench logits32 --rows 160
-    python -m whisper_trt_b200.kernel_bench prompt --rows 80 --tokens 224 --cached 0
-    python -m whisper_trt_b200.kernel_bench cross --windows 32 --beams 5
-    python -m whisper_trt_b200.kernel_bench self_step --rows 160 --cache-lo 4 --cache-hi 224
-    python -m whisper_trt_b200.kernel_bench dec_linear --rows 160
+    python benchmarks/kernel_bench.py beam_scores --windows 32 --beams 5 [--timestamps] [--reps 20]
+    python benchmarks/kernel_bench.py logits32 --rows 160
+    python benchmarks/kernel_bench.py prompt --rows 80 --tokens 224 --cached 0
+    python benchmarks/kernel_bench.py cross --windows 32 --beams 5
+    python benchmarks/kernel_bench.py self_step --rows 160 --cache-lo 4 --cache-hi 224
+    python benchmarks/kernel_bench.py dec_linear --rows 160
 
-(from the ``whisper-trt_b200`` directory, or with it on PYTHONPATH). Inputs are seeded N(0, 1) (weights N(0, 0.02));
+(from the repository root). Inputs are seeded N(0, 1) (weights N(0, 0.02));
 several layers' worth of inputs rotate so that consecutive calls do not hit L2 for the bytes they stream.
 """
 
@@ -16,12 +16,16 @@ from __future__ import annotations
 
 import argparse
 import json
+import sys
+from pathlib import Path
 from types import SimpleNamespace
 
 import torch
 
-from . import attn_plugin as ap
-from . import slots
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent / "whisper-trt_b200"))
+
+from whisper_trt_b200 import attn_plugin as ap  # noqa: E402
+from whisper_trt_b200 import slots  # noqa: E402
 
 
 def _time(fn, reps: int) -> float:
@@ -151,8 +155,8 @@ def dec_linear(a) -> dict:
     h = ln_linear(x, 4d, gelu), y += fc2(h) -- each timed alone and the six in sequence. Each op rotates through
     enough weight copies (>= 256 MB, twice the L2) that its weights stream from HBM, as a decoder step's 32 layers'
     weights do. Bytes: weights + biases + the rows read and written."""
-    from . import _lib
-    from . import decoder_kernels as dk
+    from whisper_trt_b200 import _lib
+    from whisper_trt_b200 import decoder_kernels as dk
 
     _lib.set_launch_flags(_lib.WT_LAUNCH_PDL)  # (as the decoder step launches them)
     dev, n, d = "cuda", a.rows, a.d_model

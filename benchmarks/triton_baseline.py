@@ -1,7 +1,7 @@
 """The reference's own Triton kernels, timed on the same GPU as this package's kernels, on the same inputs -- the
 GPU baseline beside ``bench.py`` (whose reference arm is the reference's CPU op bodies).
 
-    python -m whisper_trt_b200.triton_baseline --ref baseline/_ref [--sections step,logits32,prompt,beam,decoder]
+    python benchmarks/triton_baseline.py --ref baseline/_ref [--sections step,logits32,prompt,beam,decoder]
 
 ``--ref`` is a directory holding the reference's ``whisper_trt`` package, unmodified (its ``attn_plugin``,
 ``beam_kernels`` and ``decoder_kernels`` need only torch and Triton). When it is missing the module prints one
@@ -32,6 +32,8 @@ from pathlib import Path
 from types import SimpleNamespace
 
 import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent / "whisper-trt_b200"))
 
 H, D, T, L = 20, 64, 1500, 32
 
@@ -303,7 +305,7 @@ def main() -> None:
     from whisper_trt import beam_kernels as RB
     from whisper_trt import decoder_kernels as RD
 
-    from . import _lib, attn_plugin, decoder_kernels, slots
+    from whisper_trt_b200 import _lib, attn_plugin, decoder_kernels, slots
 
     _lib.set_launch_flags(_lib.WT_LAUNCH_PDL)  # (as the decoder step launches this package's kernels)
     ours = SimpleNamespace(attn_plugin=attn_plugin, decoder_kernels=decoder_kernels, slots=slots)

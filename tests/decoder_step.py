@@ -20,7 +20,7 @@ from typing import Callable
 import torch
 import torch.nn.functional as F
 
-from . import attn_plugin
+from whisper_trt_b200 import attn_plugin
 
 
 @dataclass(frozen=True)

@@ -3,7 +3,7 @@ bookkeeping, on CPU) on the seeded cases of ``cases.py``.
 
 Run where the reference source tree is importable (it does not travel to the GPU box; the fixtures do):
 
-    python tests/golden/make_golden.py [--reference-src <path to the reference's src/ directory>]
+    python tests/golden/make_golden.py --reference-src <path to the reference's src/ directory>
 
 Writes ``attn_golden.npz`` (attention outputs + input digests), ``slots_golden.npz`` (per-step search states
 before/after the reference's bookkeeping), ``scores_golden.npz`` (beam scoring) and ``decoder_golden.npz`` (the
@@ -273,7 +273,7 @@ def decoder_golden(ref_src: str) -> dict:
 
 def main() -> None:
     ap_ = argparse.ArgumentParser()
-    ap_.add_argument("--reference-src", default="/root/reference/src")
+    ap_.add_argument("--reference-src", required=True)
     ap_.add_argument("--only", choices=["decoder"], default=None, help="write only this fixture")
     args = ap_.parse_args()
     sys.path.insert(0, args.reference_src)

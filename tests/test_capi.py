@@ -213,6 +213,6 @@ def test_triton_baseline_without_the_reference(tmp_path):
     import sys
 
     root = Path(__file__).resolve().parent.parent
-    out = subprocess.run([sys.executable, "-m", "whisper_trt_b200.triton_baseline", "--ref", str(tmp_path)],
-                         cwd=root / "whisper-trt_b200", capture_output=True, text=True, timeout=300, check=True)
+    out = subprocess.run([sys.executable, str(root / "benchmarks" / "triton_baseline.py"), "--ref", str(tmp_path)],
+                         cwd=root, capture_output=True, text=True, timeout=300, check=True)
     assert "unavailable" in json.loads(out.stdout.strip().splitlines()[-1])

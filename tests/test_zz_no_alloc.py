@@ -4,14 +4,17 @@
 plugin enqueue that has to stay inside the memory its engine planned, or an application whose device memory is
 owned by its own allocator. It keeps its scratch in a fixed 8 MiB device array inside the library instead of a
 caller-given workspace. Each check below calls it through the C ABI (ctypes, raw pointers) twice in a row and
-compares its output with ``wt_cross_attn`` (the entry point with a workspace) on the same inputs, within the
-attention tolerance of the other tests (max-abs 2e-3). This file is collected last on purpose.
+compares its output with ``wt_cross_attn`` (the entry point with a workspace) on the same inputs and with the CPU
+oracle (``oracle.attn.cross_attn``, the reference op body restated), both within the attention tolerance of the
+other tests (max-abs 2e-3): the two entry points run different kernels, so the oracle catches an error common to
+both. This file is collected last on purpose.
 """
 
 import numpy as np
 import pytest
 import torch
 
+from oracle import attn as oracle
 from whisper_trt_b200 import _lib
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
@@ -48,7 +51,15 @@ def _no_alloc(lib, code, q, k, v):
     return y
 
 
-@pytest.mark.parametrize("shape", [(8, 5, 20, 1500), (2, 5, 20, 1500), (3, 20, 4, 700)])
+def _oracle(q, k, v):
+    return torch.from_numpy(oracle.cross_attn(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                              v.float().cpu().numpy()))
+
+
+# (windows, queries per window, heads, frames): whisper's 5 beams over 1500 frames; 20 queries (three 8-query tiles);
+# 40 queries (two query groups) over frames that are not a multiple of the key slices or of 16; a 17-frame window
+@pytest.mark.parametrize("shape", [(8, 5, 20, 1500), (2, 5, 20, 1500), (3, 20, 4, 700), (2, 40, 4, 333),
+                                   (1, 5, 20, 17)])
 def test_no_alloc_matches_workspace_entry_point_twice(shape):
     lib = _lib.load()
     for call in range(2):  # two calls in a row: the second starts from the array the first left behind
@@ -58,6 +69,8 @@ def test_no_alloc_matches_workspace_entry_point_twice(shape):
         torch.cuda.synchronize()
         err = (out.float() - ref.float()).abs().max().item()
         assert np.isfinite(err) and err <= ATOL, (call, err)
+        err_oracle = (out.float().cpu() - _oracle(q, k, v)).abs().max().item()
+        assert np.isfinite(err_oracle) and err_oracle <= ATOL, (call, err_oracle)
 
 
 def test_no_alloc_bf16():
@@ -69,6 +82,8 @@ def test_no_alloc_bf16():
         torch.cuda.synchronize()
         bound = ATOL + 2.0**-8 * ref.float().abs()
         assert ((out.float() - ref.float()).abs() <= bound).all()
+        exact = _oracle(q, k, v)
+        assert ((out.float().cpu() - exact).abs() <= ATOL + 2.0**-8 * exact.abs()).all()
 
 
 def test_no_alloc_rejects_shapes_beyond_its_scratch():

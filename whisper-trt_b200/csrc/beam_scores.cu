@@ -773,11 +773,8 @@ template <int KK, bool TS>
 int launch_scores(const ScoreArgs &a, int n, void *stream) {
   auto kernel = beam_scores_kernel<KK, TS>;
   const int smem = a.cap * static_cast<int>(sizeof(float) + sizeof(int));
-  static int attr_bytes = 0;
-  if (smem > attr_bytes) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_bytes = smem;
-  }
+  const int st = opt_in_smem<beam_scores_kernel<KK, TS>>(smem, "beam_scores");
+  if (st != WT_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n * kScoreCluster);
   cfg.blockDim = dim3(kScoreThreads);

@@ -25,6 +25,32 @@ int launch_flags() { return g_launch_flags.load(std::memory_order_relaxed); }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+int current_device(int *dev, const char *what) {
+  const cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return fail(WT_ERR_CUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  if (*dev < 0 || *dev >= kMaxDevices)
+    return fail(WT_ERR_CUDA, "%s: device %d is beyond the %d this library tracks", what, *dev, kMaxDevices);
+  return WT_OK;
+}
+
+namespace {
+std::atomic<int> g_sm_counts[kMaxDevices];
+}  // namespace
+
+int device_sm_count() {
+  int dev = 0;
+  if (current_device(&dev, "sm count") != WT_OK) return 0;
+  int n = g_sm_counts[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  const cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess || n <= 0) {
+    fail(WT_ERR_CUDA, "sm count: cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    return 0;
+  }
+  g_sm_counts[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
 }  // namespace wt
 
 extern "C" {

@@ -6,7 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
+#include <mutex>
 
 #include "whisper_attn_b200.h"
 
@@ -16,6 +18,38 @@ namespace wt {
 int fail(int status, const char *fmt, ...);  // records the calling thread's message, returns status
 int launch_flags();
 bool aligned16(const void *p);
+
+// ---- per-device queries and settings (thread safe) -------------------------------------------------------
+constexpr int kMaxDevices = 64;
+// The calling thread's current device into *dev; WT_ERR_CUDA (message recorded) if it cannot be read or is beyond
+// kMaxDevices.
+int current_device(int *dev, const char *what);
+// The current device's SM count, queried once per device; 0 (message recorded) if the query fails.
+int device_sm_count();
+
+// Let `Kernel` launch with `bytes` of dynamic shared memory on the current device. The attribute is per device, so
+// it is set once per (kernel, device) and again only for a larger size; the recorded size only grows, under a lock,
+// so concurrent first calls from several host threads (or several devices driven by one process) stay correct.
+// WT_ERR_CUDA with the runtime's message when the device refuses the size.
+template <auto Kernel>
+int opt_in_smem(int bytes, const char *what) {
+  static std::atomic<int> granted[kMaxDevices];
+  static std::mutex mu;
+  int dev = 0;
+  const int st = current_device(&dev, what);
+  if (st != WT_OK) return st;
+  if (granted[dev].load(std::memory_order_acquire) >= bytes) return WT_OK;
+  std::lock_guard<std::mutex> lock(mu);
+  if (granted[dev].load(std::memory_order_relaxed) >= bytes) return WT_OK;
+  const cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // (clear it: the next launch must not report this error as its own)
+    return fail(WT_ERR_CUDA, "%s: cannot opt into %d bytes of dynamic shared memory on device %d: %s", what, bytes,
+                dev, cudaGetErrorString(e));
+  }
+  granted[dev].store(bytes, std::memory_order_release);
+  return WT_OK;
+}
 
 #define WT_REQUIRE(cond, status, ...)            \
   do {                                           \

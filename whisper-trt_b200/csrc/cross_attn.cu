@@ -238,7 +238,8 @@ int query_tiles(int S) {
 int fused_splits(int W, int S, int H, int Tn) {
   const int nt = query_tiles(S);
   const long long units = static_cast<long long>(W) * H * ((S + nt * 8 - 1) / (nt * 8));
-  const long long target = 148LL * 8;
+  const int sms = device_sm_count();
+  const long long target = static_cast<long long>(sms > 0 ? sms : 148) * 8;
   long long p = (target + units - 1) / units;
   const long long blocks = (Tn + 15) / 16;
   long long cap = blocks / (2 * kCrossWarps);

@@ -467,27 +467,20 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   }
 }
 
-int g_sm_count[64] = {};
-
+// The SM count the plan is sized for (148 on a B200 if the device cannot be queried: the launch then reports the
+// device's own error).
 int sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (g_sm_count[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_sm_count[dev] = n;
-  }
-  return g_sm_count[dev];
+  const int n = device_sm_count();
+  return n > 0 ? n : 148;
 }
 
 // A launch shape forced by the WT_CROSS_SHAPE environment variable (a tuning knob), or -1.
 int forced_shape() {
-  static int idx = -2;
-  if (idx == -2) {
+  static const int idx = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_CROSS_SHAPE");
     const int v = e ? atoi(e) : -1;
-    idx = (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : -1;
-  }
+    return (v >= 0 && v < static_cast<int>(sizeof(kShapes) / sizeof(kShapes[0]))) ? v : -1;
+  }();
   return idx;
 }
 
@@ -525,12 +518,8 @@ StreamPlan plan_stream(int W, int S, int H, int Tn) {
 template <typename T, int NT, int WARPS, int STAGES, bool PAIR, int CTAS>
 int launch_stream_shape(const CUtensorMap &km, const CUtensorMap &vm, const StreamArgs &a, int grid, void *stream) {
   constexpr int smem = smem_bytes(WARPS, STAGES);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(cross_stream_kernel<T, NT, WARPS, STAGES, PAIR, CTAS>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  const int st = opt_in_smem<cross_stream_kernel<T, NT, WARPS, STAGES, PAIR, CTAS>>(smem, "cross_attn");
+  if (st != WT_OK) return st;
   return launch("cross_attn", cross_stream_kernel<T, NT, WARPS, STAGES, PAIR, CTAS>, dim3(grid), dim3((WARPS + 1) * 32), smem,
                 stream, km, vm, a);
 }

@@ -72,34 +72,31 @@ struct DlPlan {
 
 // The most k splits a GEMM may take: WT_DL_MAX_SPLITS (a tuning knob), else kDlMaxSplits.
 int max_splits() {
-  static int v = 0;
-  if (v == 0) {
+  static const int v = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_DL_MAX_SPLITS");
     const int x = e ? atoi(e) : kDlMaxSplits;
-    v = (x >= 1 && x <= kDlMaxSplits) ? x : kDlMaxSplits;
-  }
+    return (x >= 1 && x <= kDlMaxSplits) ? x : kDlMaxSplits;
+  }();
   return v;
 }
 
 // Row chunks per 256 rows forced by WT_DL_CHUNKS (a tuning knob, 1-4), else 0 (chosen by the cost model).
 int row_chunks() {
-  static int v = -1;
-  if (v < 0) {
+  static const int v = [] {
     const char *e = getenv("WT_DL_CHUNKS");
     const int x = e ? atoi(e) : 0;
-    v = (x >= 1 && x <= 4) ? x : 0;
-  }
+    return (x >= 1 && x <= 4) ? x : 0;
+  }();
   return v;
 }
 
 // WT_DL_TRACE=1: print every plan the chooser weighs to stderr (a tuning aid; off by default).
 bool trace_plans() {
-  static int v = -1;
-  if (v < 0) {
+  static const bool v = [] {
     const char *e = getenv("WT_DL_TRACE");
-    v = (e != nullptr && e[0] == '1') ? 1 : 0;
-  }
-  return v == 1;
+    return e != nullptr && e[0] == '1';
+  }();
+  return v;
 }
 
 int min_chunks(int N) { return (N + kDlMaxRows - 1) / kDlMaxRows; }
@@ -536,16 +533,11 @@ __global__ void __launch_bounds__(128)
   }
 }
 
-int g_dl_sm[64] = {};
+// The SM count the plan is sized for (148 on a B200 if the device cannot be queried: the launch then reports the
+// device's own error).
 int dl_sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (g_dl_sm[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_dl_sm[dev] = n;
-  }
-  return g_dl_sm[dev];
+  const int n = device_sm_count();
+  return n > 0 ? n : 148;
 }
 
 // Thread-block clusters of `splits` CTAs of `kernel` (with `smem` bytes each) resident at once on this device --
@@ -641,24 +633,21 @@ int launch_gemm(int dtype, const void *x, const void *w, const void *b, const vo
   auto kernel = dec_gemm_kernel<T, MODE>;
   // (per instantiation, once per device: the largest dynamic shared memory the device lets a block opt into, less
   // the kernel's static shared memory; every plan stays below it, and the cluster-occupancy query needs it set)
-  static bool smem_set[64] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !smem_set[dev]) {
-    int optin = 0;
-    cudaFuncAttributes fa{};
-    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncGetAttributes(&fa, kernel) != cudaSuccess ||
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - static_cast<int>(fa.sharedSizeBytes)) != cudaSuccess)
-      return fail(WT_ERR_CUDA, "dec_linear: cannot opt into %d bytes of shared memory: %s", optin,
-                  cudaGetErrorString(cudaGetLastError()));
-    smem_set[dev] = true;
-  }
+  int st = current_device(&dev, "dec_linear");
+  if (st != WT_OK) return st;
+  int optin = 0;
+  cudaFuncAttributes fa{};
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+      cudaFuncGetAttributes(&fa, kernel) != cudaSuccess)
+    return fail(WT_ERR_CUDA, "dec_linear: cannot read the shared-memory limits: %s",
+                cudaGetErrorString(cudaGetLastError()));
+  st = opt_in_smem<dec_gemm_kernel<T, MODE>>(optin - static_cast<int>(fa.sharedSizeBytes), "dec_linear");
+  if (st != WT_OK) return st;
   const DlPlan p = tuned_plan(kernel, N, V, K, ln);
   CUtensorMap wm, xm;
-  int st = encode_tile_map(&wm, w, static_cast<unsigned long long>(V), static_cast<unsigned long long>(K), kDlTileV,
-                           dtype);
+  st = encode_tile_map(&wm, w, static_cast<unsigned long long>(V), static_cast<unsigned long long>(K), kDlTileV,
+                       dtype);
   if (st != WT_OK) return st;
   st = encode_tile_map(&xm, x, static_cast<unsigned long long>(N), static_cast<unsigned long long>(K), p.nmma, dtype);
   if (st != WT_OK) return st;

@@ -145,8 +145,6 @@ __global__ void __launch_bounds__(kLgThreads)
   if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(2 * tcols));
 }
 
-int g_lg_sm[64] = {};
-
 }  // namespace
 }  // namespace wt
 
@@ -178,16 +176,11 @@ extern "C" int wt_logits32(int dtype, const void *x, const void *w, float *y, in
   const int smem = 1024 + stages * stage_bytes + (2 * stages + 4) * 8 + 16;
   const int kblocks = (d_model + kLgKBlock - 1) / kLgKBlock;
   auto kernel = dtype == WT_BF16 ? logits_kernel<true> : logits_kernel<false>;
-  static int attr_bytes[2] = {0, 0};
-  if (smem > attr_bytes[dtype]) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_bytes[dtype] = smem;
-  }
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
-    if (g_lg_sm[dev] == 0) cudaDeviceGetAttribute(&g_lg_sm[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (g_lg_sm[dev] > 0) sms = g_lg_sm[dev];
-  }
+  st = dtype == WT_BF16 ? opt_in_smem<logits_kernel<true>>(smem, "logits32")
+                        : opt_in_smem<logits_kernel<false>>(smem, "logits32");
+  if (st != WT_OK) return st;
+  const int sms = device_sm_count();
+  if (sms <= 0) return WT_ERR_CUDA;
   const int tiles = ((vocab + kLgTileV - 1) / kLgTileV) * chunks;
   const int grid = tiles < sms ? tiles : sms;
   return launch("logits32", kernel, dim3(grid), dim3(kLgThreads), smem, stream, wm, xm, y, rows, vocab, kblocks,

@@ -331,11 +331,8 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
   const int cap = (C + splits - 1) / splits;
   const int smem = kWarpsPerCta * ring_bytes<U, kStages>() + (cap * 4 + 15) / 16 * 16;
   auto kernel = self_step_kernel<T, D, U, kStages>;
-  static int attr_bytes = 0;
-  if (smem > attr_bytes) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_bytes = smem;
-  }
+  const int st = opt_in_smem<self_step_kernel<T, D, U, kStages>>(smem, "self_attn_step");
+  if (st != WT_OK) return st;
   int *counters = nullptr;
   float *part = nullptr;
   if (splits > 1) {
@@ -356,12 +353,11 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
 // U[224, 447], against 1674 with (2, 3)). WT_SELF_SHAPE (a tuning knob) forces 0 = (4, 2), 1 = (2, 2), 2 = (2, 3) or
 // 3 = (1, 4).
 int self_shape(int cap) {
-  static int forced = -2;
-  if (forced == -2) {
+  static const int forced = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_SELF_SHAPE");
     const int x = e ? atoi(e) : -1;
-    forced = (x >= 0 && x <= 3) ? x : -1;
-  }
+    return (x >= 0 && x <= 3) ? x : -1;
+  }();
   if (forced >= 0) return forced;
   return cap <= 256 ? 2 : 0;
 }
@@ -394,7 +390,8 @@ int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim) {
   // pairs alone would leave the SMs short of CTAs (< 2 per SM): splitting costs a partial and a combine
   const long long items = static_cast<long long>(rows) * heads;
   long long s = (capacity + wt::kMaxSplitKeys - 1) / wt::kMaxSplitKeys;
-  const long long want = (148LL * 2 + items - 1) / items;
+  const int sms = wt::device_sm_count();
+  const long long want = (static_cast<long long>(sms > 0 ? sms : 148) * 2 + items - 1) / items;
   if (want > s) s = want;
   const long long cap = (capacity + 63) / 64;  // at least ~64 keys (16 per warp) per split
   if (s > cap) s = cap;

@@ -262,11 +262,8 @@ int launch_prefill(const void *qkv, const void *kc, const void *vc, const int64_
                    void *y, int N, int S, int H, int C, void *stream) {
   auto kernel = self_prefill_kernel<T>;
   const int smem = kPFixedSmem + ((C * 4 + 127) / 128) * 128;
-  static int attr_bytes = 0;
-  if (smem > attr_bytes) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_bytes = smem;
-  }
+  const int st = opt_in_smem<self_prefill_kernel<T>>(smem, "self_attn");
+  if (st != WT_OK) return st;
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(kPD)) * 1.4426950408889634);
   return launch("self_attn", kernel, dim3(N * H, (S + kPQ - 1) / kPQ), dim3(kPThreads), smem, stream,
                 static_cast<const T *>(qkv), static_cast<const T *>(kc), static_cast<const T *>(vc), offset, src,

@@ -96,3 +96,11 @@ def linear_residual(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, res: torc
                                     n, k, ws.data_ptr(), ws.numel(), _stream(dev))
     _lib.check(st, what)
     return y
+
+
+def install(module) -> None:
+    """Route a reference ``whisper_trt.decoder_kernels`` module's launchers to these kernels (in place), so that its
+    callers -- ``TritonDecoderBackend.step_fn``'s ``run`` and ``run_cublas`` (runtime.py:134-167) -- run on them
+    unchanged. The module's other names (its Triton kernels, ``triton``) are left as they are."""
+    for name in ("layer_norm_bias", "ln_linear", "linear_residual"):
+        setattr(module, name, globals()[name])

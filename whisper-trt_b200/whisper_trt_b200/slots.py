@@ -188,3 +188,11 @@ def step_bookkeeping(s, logits: torch.Tensor, ns: torch.Tensor) -> None:
     the [N, V] scores."""
     top_s, top_i = best(s, logits, ns)
     update(s, top_s, top_i, ns)
+
+
+def install(module) -> None:
+    """Route a reference ``whisper_trt.beam_kernels`` module's beam-mode bookkeeping (``scores``, ``update``) to
+    these kernels (in place), so that the reference's ``Search._body`` (search.py:251-256, ``fused=True``) runs on them
+    unchanged. Sampled slots (``sampling_slots=True``) are refused by :func:`update`."""
+    for name in ("scores", "update"):
+        setattr(module, name, globals()[name])
