@@ -12,10 +12,15 @@ synthetic tensors of whisper-large-v3's shapes (20 heads x 64, 1500 frames) resi
 several GB, far more than the 126 MB L2, so no flush is needed between steps.
 
 value = algorithmic HBM bytes per step (see ``step_bytes``) x steps / time, summed over all GPUs (GB/s, whole job);
-ms_per_step = the max over ranks of the device time per step. Prints one JSON line on rank 0.
+ms_per_step = the max over ranks of the device time per step. Prints one JSON line on rank 0, with: ``e2e`` (the
+same step through the public API with its inputs copied in from pinned host memory and its outputs copied out, and
+the copy rate each rank gets); ``roofline`` (the dominant kernel's achieved bandwidth); ``also`` (configs 2, 4 and
+5 at the same N); at N = 1 ``vs_reference_gpu`` (the reference's own Triton kernels timed beside these on the same
+inputs) and ``cpu_baseline``.
 
-``--impl reference``: the reference's CPU implementation of the path (its PyTorch-eager ops restated in numpy:
-``oracle/``) on the host cores, a bounded sample per step (one layer of a block of windows), same metric.
+``--impl reference``: the reference's CPU implementation of the path on the host cores -- its own PyTorch ops,
+imported unmodified from ``baseline/_ref`` (their numpy restatement in ``oracle/`` when it is not staged) -- a
+bounded sample per step (one layer of a block of windows), same metric and config.
 """
 
 from __future__ import annotations
@@ -55,9 +60,12 @@ WORKLOADS = {
                     "(C = 228), random parent reorder + append every step, windows replaced (fresh length 4) with "
                     "p = 0.02 per step"),
     # 16 slots x 5 samples, identity reorder, 224-token prompt prefix, lengths U[224, 447], C = 448
+    # (the prompt prefix prefilled once per window in its first row and shared by the window's samples through the
+    # slot table, as the reference's prefilled Search lays it out: search.py:440-443)
     "config4": dict(windows=16, beams=5, capacity=448, off_lo=224, off_hi=447, refill_p=0.0, advance=True,
-                    reorder="identity", refill_to=224, episode=224, desc="config 4: 16 slots x 5 samples = 80 rows, identity reorder, "
-                    "224-token prompt prefix, lengths U[224, 447] (C = 448)"),
+                    reorder="identity", refill_to=224, episode=224, prefix=224, prefilled=True,
+                    desc="config 4: 16 slots x 5 samples = 80 rows, identity reorder, 224-token prompt prefix shared "
+                    "through the slot table, lengths U[224, 447] (C = 448)"),
     # 64 slots x beam 5 per GPU, U[4, 448], C = 448
     "config5": dict(windows=64, beams=5, capacity=448, off_lo=4, off_hi=447, refill_p=0.0, advance=True,
                     reorder="perm", refill_to=4, episode=200, desc="config 5: 64 slots x beam 5 = 320 rows per GPU, cache lengths U[4, 448] "
@@ -80,6 +88,7 @@ class Schedule:
         rng = np.random.default_rng(seed)
         W, K, C = wl["windows"], wl["beams"], wl["capacity"]
         self.W, self.K, self.C, self.n = W, K, C, n_steps
+        self.prefix = wl.get("prefix", 0)  # slots every row of a window reads from the window's first row
 
         def draw():
             return rng.integers(wl["off_lo"], wl["off_hi"] + 1, W).astype(np.int64)
@@ -106,28 +115,48 @@ class Schedule:
                 pos = np.where(self.refill[s], self.refill_pos[s], pos + (1 if wl["advance"] else 0))
         self.pos[n_steps] = pos
 
-    def step_bytes(self, s: int, windows: slice | None = None) -> int:
-        """Algorithmic HBM bytes of step s (all 32 layers): per layer sum_rows off*(5120+4) + rows*20480 +
-        windows*7.68e6 (K/V of the cached positions, the slot table, qkv/append/outputs, the cross K/V)."""
+    def kv_positions(self, p: np.ndarray, unique: bool = True) -> int:
+        """(row, cached position) pairs whose K/V a layer reads for windows at offsets ``p``: every row's own, or,
+        ``unique``, a shared prompt prefix once per window (its rows read it from the window's first row)."""
+        if not unique or not self.prefix:
+            return int(p.sum()) * self.K
+        shared = np.minimum(p, self.prefix)
+        return int(shared.sum() + self.K * (p - shared).sum())
+
+    def step_bytes(self, s: int, windows: slice | None = None, unique: bool = True) -> int:
+        """Algorithmic HBM bytes of step s (all 32 layers): per layer K/V of the cached positions (5120 B each; a
+        shared prefix once per window when ``unique``) + the slot table (4 B per row and position) + rows*20480
+        (qkv/append/outputs) + windows*7.68e6 (the cross K/V)."""
         p = self.pos[s] if windows is None else self.pos[s][windows]
         rows = p.size * self.K
-        return L * (int(p.sum()) * self.K * (KV_ROW_BYTES + SRC_BYTES) + rows * FIXED_ROW_BYTES
-                    + p.size * CROSS_WINDOW_BYTES)
+        return L * (self.kv_positions(p, unique) * KV_ROW_BYTES + int(p.sum()) * self.K * SRC_BYTES
+                    + rows * FIXED_ROW_BYTES + p.size * CROSS_WINDOW_BYTES)
 
     def cross_launch_bytes(self) -> int:
         return self.W * CROSS_WINDOW_BYTES + self.W * self.K * (2560 + 2560)
 
-    def self_launch_bytes(self, s: int) -> int:
-        return int(self.pos[s].sum()) * self.K * (KV_ROW_BYTES + SRC_BYTES) + self.W * self.K * (7680 + 5120 + 2560)
+    def self_launch_bytes(self, p: np.ndarray, append: bool) -> int:
+        """One self-attention launch at offsets ``p``: K/V (unique) + slot table + qkv in + output (+ the append)."""
+        return (self.kv_positions(p) * KV_ROW_BYTES + int(p.sum()) * self.K * SRC_BYTES
+                + self.W * self.K * (7680 + 2560 + (5120 if append else 0)))
 
 
-def initial_src(W: int, K: int, C: int, seed: int) -> np.ndarray:
-    """The slot tables at the start: each slot column of a window a random permutation of its beams' rows -- what
-    random parent permutations produce -- so every row reads distinct cache rows (no two rows of a window share a
-    (row, slot), so the bytes counted are the bytes the kernels must fetch)."""
-    rng = np.random.default_rng(seed + 7)
-    perm = np.argsort(rng.random((W, C, K)), axis=2)  # [W, C, K]: a permutation of the K beams per (window, slot)
-    rows = (np.arange(W)[:, None, None] * K + perm).transpose(0, 2, 1).reshape(W * K, C)
+def initial_src(W: int, K: int, C: int, seed: int, wl: dict | None = None) -> np.ndarray:
+    """The slot tables at the start. Beam workloads: each slot column of a window a random permutation of its
+    beams' rows -- what random parent permutations produce -- so every row reads distinct cache rows (no two rows of
+    a window share a (row, slot): the bytes counted are the bytes the kernels must fetch). Identity reorder (sampled
+    rows): each row its own. A prompt prefix (``wl["prefix"]`` slots) is read by every row of a window from the
+    window's first row, where the reference's prefill writes it (search.py:440-443)."""
+    wl = wl or {}
+    if wl.get("reorder", "perm") == "perm":
+        rng = np.random.default_rng(seed + 7)
+        perm = np.argsort(rng.random((W, C, K)), axis=2)  # [W, C, K]: a permutation of the K beams per (window, slot)
+        rows = (np.arange(W)[:, None, None] * K + perm).transpose(0, 2, 1).reshape(W * K, C)
+    else:
+        rows = np.repeat(np.arange(W * K)[:, None], C, axis=1)
+    prefix = min(wl.get("prefix", 0), C)
+    if prefix:
+        rows[:, :prefix] = (np.arange(W * K) // K * K)[:, None]
     return rows.astype(np.int32)
 
 
@@ -156,23 +185,52 @@ def profiled_traffic(workload: str) -> float | None:
 
 # --- clocks during the timed region --------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons of one GPU, sampled from a thread every ~2 ms through NVML (read-only queries;
+    a timed region of a few tens of ms still gets samples), else through ``nvidia-smi -lms 100``. ``stop(t0, t1)``
+    keeps the samples taken inside [t0, t1] (host wall clock)."""
+
     QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
     NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.proc = None
+        self.proc, self.thread, self.rows = None, None, []
+        try:
+            import threading
+
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+            self.stop_flag = threading.Event()
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    t = time.time()
+                    mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append((t, mhz, self.max_mhz, ["Active" if r & b else "Not Active" for b in bits]))
+                    time.sleep(0.002)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = "nvml, every ~2 ms"
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(gpu_index)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi, every 100 ms"
         except OSError:
             self.proc = None
 
-    def stop(self, t0: float, t1: float) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
+    def _smi_rows(self) -> list:
         self.proc.terminate()
         out, _ = self.proc.communicate(timeout=10)
         rows = []
@@ -186,10 +244,22 @@ class ClockSampler:
                 rows.append((ts, float(parts[2]), float(parts[3]), parts[5:9]))
             except (ValueError, IndexError):
                 continue
-        inside = [r for r in rows if t0 - 0.15 <= r[0] <= t1 + 0.15]
-        note = "samples inside the timed region"
+        return rows
+
+    def stop(self, t0: float, t1: float) -> dict:
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            rows = list(self.rows)
+        elif self.proc is not None:
+            rows = self._smi_rows()
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "no clock source"}
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        note = f"samples inside the timed region ({self.source})"
         if not inside:
-            inside, note = rows[-5:], "timed region shorter than the sampling period: last samples of the run"
+            inside = [r for r in rows if t0 - 0.15 <= r[0] <= t1 + 0.15]
+            note = f"samples within 150 ms of the timed region ({self.source})"
         if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "no samples"}
         reasons = sorted({n for r in inside for n, v in zip(self.NAMES, r[3]) if v.lower().startswith("active")})
@@ -198,7 +268,28 @@ class ClockSampler:
 
 
 # --- our arm -----------------------------------------------------------------------------------------------------
-def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+def make_config(args, wl: dict, sch: Schedule, world: int) -> dict:
+    """The ``config`` of a bench line, from rank 0's schedule (both arms print the same one for the same run)."""
+    timed = range(args.warmup, args.warmup + args.steps)
+    W, K, C = wl["windows"], wl["beams"], wl["capacity"]
+    cfg = {"workload": wl["desc"], "name": args.workload, "rows": W * K, "windows": W, "beams": K, "layers": L,
+           "heads": H, "head_dim": D, "frames": T_FRAMES, "capacity": C,
+           "mean_cached_positions": round(float(np.mean([sch.pos[s].mean() for s in timed])), 1),
+           "bytes_per_step": int(sum(sch.step_bytes(s) for s in timed) / args.steps),
+           "parallelism": f"{world} independent shards (windows per GPU), no collective on the hot path",
+           "l2": "inputs larger than L2: several GB read per step vs 126 MB L2; no flush",
+           "graph": "one CUDA graph replay per step",
+           "launch": "programmatic dependent launch" if not args.no_pdl else "plain launches"}
+    if sch.prefix:
+        cfg["prefix"] = sch.prefix
+        cfg["bytes_per_step_logical"] = int(sum(sch.step_bytes(s, unique=False) for s in timed) / args.steps)
+        cfg["bytes"] = ("unique: the shared prompt prefix counted once per window (its rows read it from the "
+                        "window's first row); bytes_per_step_logical counts it per row")
+    return cfg
+
+
+def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) -> dict | None:
+    """The workload on this rank's GPU; ``light``: the step and the per-kernel times only (no e2e leg)."""
     import torch
 
     from whisper_trt_b200 import attn_plugin as ap
@@ -220,7 +311,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     q = torch.randn(L, W, K, HD, generator=g, device=dev, dtype=torch.float16)
     y_self = torch.empty(L, N, 1, HD, device=dev, dtype=torch.float16)
     y_cross = torch.empty(L, W, K, HD, device=dev, dtype=torch.float16)
-    src0 = torch.from_numpy(initial_src(W, K, C, seed)).to(dev)
+    src0 = torch.from_numpy(initial_src(W, K, C, seed, wl)).to(dev)
     src = src0.clone()
     pos = torch.from_numpy(sch.pos[0].copy()).to(dev)
     offset = pos.repeat_interleave(K).contiguous()
@@ -243,7 +334,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     def tail():
         """The step's bookkeeping from its schedule row (parent_cur .. rpos_cur): window replacements, then the
         parents' slot-table reorder and the offsets' advance."""
-        sl.slot_reset(src, slots_cur.view(W), K, prefilled=False)
+        sl.slot_reset(src, slots_cur.view(W), K, prefilled=wl.get("prefilled", False))
         torch.where(mask_cur.view(W), rpos_cur.view(W), pos, out=pos)
         sl.beam_reorder(src, parent_cur.view(W, K), pos, live=live_cur.view(W), offset=offset,
                         advance=wl["advance"])
@@ -306,19 +397,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     elapsed_ms = ev0.elapsed_time(ev1)
     timed = range(args.warmup, args.warmup + args.steps)
     my_bytes = sum(sch.step_bytes(s) for s in timed)
-    mean_off = float(np.mean([sch.pos[s].mean() for s in timed]))
     t_max, total_bytes = combine_ranks(elapsed_ms, my_bytes, dist, dev)
     ms_per_step = t_max / args.steps
     value = total_bytes / (t_max * 1e-3) / 1e9
 
     # per-kernel device times (roofline): eager launches bracketed by events, queued behind a sleep so the
     # host stays ahead of the GPU
-    ker = kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src)
+    ker = kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch)
 
     # end to end through the public API: H2D of the step's inputs from pinned memory, the step, D2H of its outputs
-    cur = {"parent": parent_cur, "slots": slots_cur, "mask": mask_cur, "live": live_cur, "rpos": rpos_cur}
-    e2e = run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, args.steps, reset_state, sch, args.warmup,
-                  dist)
+    e2e = None
+    if not light:
+        cur = {"parent": parent_cur, "slots": slots_cur, "mask": mask_cur, "live": live_cur, "rpos": rpos_cur}
+        e2e = run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, args.steps, reset_state, sch,
+                      args.warmup, dist)
 
     peak, peak_kind = measured_hbm_peak()
     cross_bytes = sch.cross_launch_bytes()
@@ -329,15 +421,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "us_per_step": round(ms_per_step * 1e3, 1),
         "rows_steps_per_s": round(N * world * args.steps / (t_max * 1e-3), 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "accumulate": "f32",
-        "data": "synthetic: seeded N(0,1) fp16 caches / cross K/V / qkv / queries (random init; no checkpoint or "
-                "dataset), seeded schedule of parents and window replacements",
-        "config": {"workload": wl["desc"], "name": args.workload, "rows": N, "windows": W, "beams": K,
-                   "layers": L, "heads": H, "head_dim": D, "frames": T_FRAMES, "capacity": C,
-                   "mean_cached_positions": round(mean_off, 1), "bytes_per_step": int(my_bytes / args.steps),
-                   "parallelism": f"{world} independent shards (windows per GPU), no collective on the hot path",
-                   "l2": f"inputs larger than L2: {my_bytes / args.steps / 1e9:.2f} GB read per step vs 126 MB L2; "
-                         "no flush", "graph": "one CUDA graph replay per step",
-                   "launch": "programmatic dependent launch" if not args.no_pdl else "plain launches"},
+        "data": DATA,
+        "config": make_config(args, wl, Schedule(wl, n_sched, shard_seed(0), start=args.warmup), world),
         "frac_of_hbm_peak": round(value / world / peak, 4), "hbm_peak_gbs": peak, "hbm_peak_kind": peak_kind,
         "roofline": {"bound": "hbm", "kernel": "cross_attn (fused split + combine)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -347,8 +432,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                      "self_attn": {"launch_us": round(ker["self_ms"] * 1e3, 2),
                                    "achieved": round(ker["self_bytes"] / (ker["self_ms"] * 1e-3) / 1e9, 1),
                                    "frac": round(ker["self_bytes"] / (ker["self_ms"] * 1e-3) / 1e9 / peak, 4)}},
-        "e2e": e2e, "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
     }
+    if e2e is not None:
+        res["e2e"] = e2e
     if L != 32:
         res["note"] = f"profiling case: {L} layers per step instead of the workload's 32 (not a bench value)"
     return res
@@ -383,7 +470,7 @@ def gpu_index(local_rank: int) -> int:
     return local_rank
 
 
-def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, reps: int = 3) -> dict:
+def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch, reps: int = 3) -> dict:
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps * L)]
     torch.cuda.synchronize(dev)
     torch.cuda._sleep(200_000_000)
@@ -398,9 +485,8 @@ def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, 
     torch.cuda.synchronize(dev)
     self_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in evs]))
     cross_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs]))
-    offs = offset.cpu().numpy()
-    self_bytes = int(offs.sum()) * (KV_ROW_BYTES + SRC_BYTES) + offs.size * (7680 + 2560)  # (no append here)
-    return {"self_ms": self_ms, "cross_ms": cross_ms, "self_bytes": self_bytes}
+    offs = offset.cpu().numpy()[:: sch.K]  # (a window's rows share its offset)
+    return {"self_ms": self_ms, "cross_ms": cross_ms, "self_bytes": sch.self_launch_bytes(offs, append=False)}
 
 
 def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_state, sch, warmup,
@@ -504,8 +590,32 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
     h2d = sum(t.numel() * t.element_size() for t in (qkv, q, *cur.values()))
     d2h = y_self.numel() * y_self.element_size() + y_cross.numel() * y_cross.element_size()
     del graphs
+    # the copy-in alone (the layers' qkv and queries, 3 steps' worth), every rank at once after a barrier: the
+    # pinned host-to-device rate each rank gets when all copy together -- the bound of the step above when the
+    # kernels keep HBM busy
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cin):
+        c0.record(cin)
+        for _ in range(3):
+            for i in range(n):
+                qkv[i].copy_(qkv_h[i], non_blocking=True)
+                q[i].copy_(q_h[i], non_blocking=True)
+        c1.record(cin)
+    torch.cuda.synchronize(dev)
+    in_bytes = qkv.numel() * qkv.element_size() + q.numel() * q.element_size()
+    copy_ms = c0.elapsed_time(c1) / 3
+    copy_max, _ = combine_ranks(copy_ms, 0, dist, dev)
     return {"value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 4),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "copy_in": {"bytes_per_step": in_bytes, "ms_per_step_all_ranks_at_once": round(copy_max, 4),
+                        "gbs_per_rank": round(in_bytes / (copy_max * 1e-3) / 1e9, 2),
+                        "gbs_whole_job": round(in_bytes * (dist.get_world_size() if dist else 1)
+                                               / (copy_max * 1e-3) / 1e9, 1),
+                        "note": "the layers' inputs copied alone from pinned host memory, every rank at once "
+                                "(slowest rank): the bound on the e2e step"},
             "path": "whisper_trt_b200.attn_plugin calls (C ABI) captured in a CUDA graph; every step the host "
                     "stages the step's schedule row, the layers' qkv / queries and the schedule are copied in from "
                     "pinned host memory and the layers' outputs copied out (per layer, on copy streams that overlap "
@@ -513,7 +623,28 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
                     "reads each step's outputs when its completion event fires"}
 
 
-# --- the reference's CPU implementation (the oracle port) ---------------------------------------------------------
+# --- the reference's CPU implementation ---------------------------------------------------------------------------
+REF_PKG = ROOT / "baseline" / "_ref"
+DATA = ("synthetic: seeded N(0,1) fp16 caches / cross K/V / qkv / queries (random init; no checkpoint or dataset), "
+        "seeded schedule of parents and window replacements")
+
+
+def reference_module():
+    """The reference's ``whisper_trt.attn_plugin``, imported unmodified from the package staged under
+    ``baseline/_ref`` (None when it is not staged). Its ops' PyTorch bodies are selected (``RUNTIME_TRITON`` off:
+    the reference's CPU path); its Triton launchers are called by name where the GPU comparison wants them."""
+    if not (REF_PKG / "whisper_trt" / "attn_plugin.py").is_file():
+        return None
+    if str(REF_PKG) not in sys.path:
+        sys.path.insert(0, str(REF_PKG))
+    try:
+        from whisper_trt import attn_plugin
+    except Exception:
+        return None
+    attn_plugin.RUNTIME_TRITON = False
+    return attn_plugin
+
+
 def cpu_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -525,29 +656,63 @@ def cpu_threads() -> int:
 
 
 class CpuSample:
-    """One layer of the workload's attention for a block of ``sw`` windows, on the host (oracle = the reference's
-    op bodies restated in numpy, float32 math on fp16 inputs)."""
+    """One layer of the workload's attention for a block of ``sw`` windows on the host cores, fp16 inputs with
+    float32 math. With the reference package staged (``kind`` "reference"): the reference's own PyTorch ops on CPU
+    tensors, in the order its TritonDecoderBackend calls them (runtime.py:139-145) -- ``self_attn`` through the slot
+    table, the cache append its Search then does for that op (search.py:249-250), ``cross_attn_split`` and
+    ``cross_attn_combine`` -- on all the host's cores (torch threads = the CPU count, under torchrun too). Without it
+    (``kind`` "port"): their numpy restatement, ``oracle/attn.py``."""
 
     def __init__(self, wl: dict, sw: int, seed: int):
-        from oracle import attn as oa
-
-        self.oa = oa
         rng = np.random.default_rng(seed)
         K, C = wl["beams"], wl["capacity"]
         self.sw, self.K, self.C = sw, K, C
         n = sw * K
-        self.qkv = rng.standard_normal((n, 1, 3 * HD), dtype=np.float32).astype(np.float16)
-        self.kc = rng.standard_normal((n, H, C, D), dtype=np.float32).astype(np.float16)
-        self.vc = rng.standard_normal((n, H, C, D), dtype=np.float32).astype(np.float16)
-        self.src = initial_src(sw, K, C, seed)
-        self.q = rng.standard_normal((sw, K, HD), dtype=np.float32).astype(np.float16)
-        self.xk = rng.standard_normal((sw, H, T_FRAMES, D), dtype=np.float32).astype(np.float16)
-        self.xv = rng.standard_normal((sw, H, T_FRAMES, D), dtype=np.float32).astype(np.float16)
+        qkv = rng.standard_normal((n, 1, 3 * HD), dtype=np.float32).astype(np.float16)
+        kc = rng.standard_normal((n, H, C, D), dtype=np.float32).astype(np.float16)
+        vc = rng.standard_normal((n, H, C, D), dtype=np.float32).astype(np.float16)
+        src = initial_src(sw, K, C, seed, wl)
+        q = rng.standard_normal((sw, K, HD), dtype=np.float32).astype(np.float16)
+        xk = rng.standard_normal((sw, H, T_FRAMES, D), dtype=np.float32).astype(np.float16)
+        xv = rng.standard_normal((sw, H, T_FRAMES, D), dtype=np.float32).astype(np.float16)
+        self.ops = reference_module()
+        if self.ops is None:
+            from oracle import attn as oa
+
+            self.kind, self.oa = "port", oa
+            self.np = (qkv, kc, vc, src, q, xk, xv)
+            self.cores = cpu_threads()
+            return
+        import torch
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.torch, self.kind, self.cores = torch, "reference", torch.get_num_threads()
+        self.qkv, self.kc, self.vc = torch.from_numpy(qkv), torch.from_numpy(kc), torch.from_numpy(vc)
+        self.src, self.q = torch.from_numpy(src), torch.from_numpy(q)
+        self.xk, self.xv = torch.from_numpy(xk), torch.from_numpy(xv)
+        self.rows = torch.arange(n)
 
     def run(self, offsets: np.ndarray) -> None:
         off = np.repeat(offsets[: self.sw], self.K)
-        self.oa.self_attn_step(self.qkv, self.kc, self.vc, off, self.src, write_cache=True)
-        self.oa.cross_attn(self.q, self.xk, self.xv)
+        if self.ops is None:
+            qkv, kc, vc, src, q, xk, xv = self.np
+            self.oa.self_attn_step(qkv, kc, vc, off, src, write_cache=True)
+            self.oa.cross_attn(q, xk, xv)
+            return
+        torch = self.torch
+        o = torch.from_numpy(off)
+        self.ops.self_attn(self.qkv, self.kc, self.vc, o, self.src)
+        ok = o < self.C
+        new = self.qkv.view(-1, 3, H, D)
+        self.kc[self.rows[ok], :, o[ok]] = new[ok, 1]
+        self.vc[self.rows[ok], :, o[ok]] = new[ok, 2]
+        self.ops.cross_attn_combine(self.ops.cross_attn_split(self.q, self.xk, self.xv), self.q)
+
+    def describe(self) -> str:
+        if self.kind == "reference":
+            return ("the reference's own PyTorch ops (whisper_trt.attn_plugin from baseline/_ref, RUNTIME_TRITON "
+                    "off: self_attn + the cache append + cross_attn_split + cross_attn_combine) on CPU tensors")
+        return "the reference's PyTorch op bodies restated in numpy (oracle/attn.py)"
 
 
 def cpu_sample_bytes(sch: Schedule, s: int, sw: int) -> int:
@@ -565,42 +730,76 @@ def run_cpu_baseline(wl: dict, sch: Schedule, min_seconds: float, sw: int) -> di
         nbytes += cpu_sample_bytes(sch, s % sch.n, sw)
         layers += 1
         s += 1
-    return {"value": round(nbytes / t_total / 1e9, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+    return {"value": round(nbytes / t_total / 1e9, 3), "unit": "GB/s", "cores": smp.cores, "kind": smp.kind,
             "host_cpus": os.cpu_count(),
-            "ms_per_step": round(t_total / layers * L * (sch.W / sw) * 1e3, 1),
             "sample": f"{layers} layer(s) of the workload's attention for {sw} of its {sch.W} windows "
-                      f"({sw * sch.K} rows: self-attention through the slot table with append + cross-attention "
-                      f"over 1500 frames), {t_total:.1f} s; ms_per_step extrapolated x32 layers x all windows"}
+                      f"({sw * sch.K} rows), {t_total:.1f} s: {smp.describe()}"}
 
 
-def run_reference(args) -> dict:
+def run_reference(args, world: int) -> dict:
+    """``--impl reference``: the reference's CPU implementation of the path on the host cores, a bounded sample per
+    step (one layer of the first ``sw`` windows at the step's offsets), same metric; value = the sample's algorithmic
+    bytes / its time."""
     wl = WORKLOADS[args.workload]
-    n_sched = args.warmup + args.steps + 4
-    sch = Schedule(wl, n_sched, 1234, start=args.warmup)
+    n_sched = args.warmup + 2 * args.steps + 4
+    sch = Schedule(wl, n_sched, shard_seed(0), start=args.warmup)
     sw = min(wl["windows"], 2)
     smp = CpuSample(wl, sw, seed=99)
     for s in range(args.warmup):
         smp.run(sch.pos[s])
-    t_total, nbytes = 0.0, 0
+    t_total, nbytes, full = 0.0, 0, 0
     for s in range(args.warmup, args.warmup + args.steps):
         t0 = time.perf_counter()
         smp.run(sch.pos[s])
         t_total += time.perf_counter() - t0
         nbytes += cpu_sample_bytes(sch, s, sw)
+        full += sch.step_bytes(s)
     value = nbytes / t_total / 1e9
-    ms_step = t_total / args.steps * L * (wl["windows"] / sw) * 1e3
-    base = {"kind": "port", "cores": cpu_threads(), "host_cpus": os.cpu_count(), "value": round(value, 3),
-            "unit": "GB/s",
-            "sample": f"per step one layer of the workload's attention for {sw} of its {wl['windows']} windows "
-                      f"({sw * wl['beams']} rows), numpy restatement of the reference's PyTorch op bodies "
-                      "(oracle/attn.py); ms_per_step extrapolated x32 layers x all windows"}
-    return {"metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "GB/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 2), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "accumulate": "f32",
-            "data": "synthetic: seeded N(0,1) fp16 inputs",
-            "config": {"workload": wl["desc"], "name": args.workload},
+    base = {"kind": smp.kind, "cores": smp.cores, "host_cpus": os.cpu_count(), "value": round(value, 3),
+            "unit": "GB/s", "sample": f"per step one layer of the workload's attention for {sw} of its "
+                                      f"{wl['windows']} windows ({sw * wl['beams']} rows): {smp.describe()}"}
+    return {"metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_total / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "accumulate": "f32",
+            "data": DATA, "config": make_config(args, wl, sch, world),
+            "extrapolated": {"sampled_layers_per_step": 1, "sampled_windows": sw, "of_layers": L,
+                             "of_windows": wl["windows"],
+                             "ms_per_full_step": round(t_total * full / nbytes / args.steps * 1e3, 1),
+                             "note": "ms_per_step is the timed sample's; the whole step (all layers and windows) "
+                                     "scaled by its algorithmic bytes is ms_per_full_step"},
             "cpu_baseline": base,
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_reference_gpu(local_rank: int, reps: int = 10) -> dict:
+    """The reference's own GPU kernels beside this package's, on this GPU and the same inputs: the decode step's
+    attention of 32 layers as its TritonDecoderBackend sequences it (self_attn_step_triton with the append, then
+    cross_attn_split_triton + cross_attn_combine_triton per layer) at config 3 and config 2, each side captured in
+    a CUDA graph (``benchmarks/triton_baseline.py``'s ``step`` section), with the clocks of the run."""
+    R = reference_module()
+    if R is None or getattr(R, "triton", None) is None:
+        return {"unavailable": "the reference package (baseline/_ref) or Triton is not available"}
+    sys.path.insert(0, str(ROOT / "benchmarks"))
+    from types import SimpleNamespace
+
+    import triton_baseline as tb
+    import torch
+
+    from whisper_trt_b200 import attn_plugin
+
+    sampler = ClockSampler(gpu_index(local_rank))
+    t0 = time.time()
+    out = {}
+    for name in ("config3", "config2"):
+        r = tb.step(R, SimpleNamespace(attn_plugin=attn_plugin), name, reps)
+        out[name] = {k: r[k] for k in ("rows", "cached_mean", "bytes_per_step", "ref_step_us", "ref_step_unsplit_us",
+                                       "ours_step_us", "ref_step_gbs", "ours_step_gbs", "speedup_vs_ref_step",
+                                       "speedup_vs_ref_step_unsplit", "max_abs_diff")}
+        torch.cuda.empty_cache()
+    out["clocks"] = sampler.stop(t0, time.time())
+    out["how"] = ("device time per step of CUDA-graph replays (10 after 3 warm-up), the same seeded inputs and static "
+                  "offsets on both sides, no bookkeeping; the reference's Triton 3.6 kernels from baseline/_ref")
+    return out
 
 
 # --- main ----------------------------------------------------------------------------------------------------
@@ -613,7 +812,10 @@ def main() -> None:
     ap_.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap_.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline sample length (rank 0, N=1)")
     ap_.add_argument("--no-cpu-baseline", action="store_true")
-    ap_.add_argument("--also", default="config2", help="a second workload reported under 'also' (N=1; '' = none)")
+    ap_.add_argument("--also", default="config2,config4,config5",
+                     help="more workloads reported under 'also', at every N (comma-separated; '' = none)")
+    ap_.add_argument("--no-ref-gpu", action="store_true",
+                     help="skip the reference's Triton kernels timed beside these (N=1, rank 0)")
     ap_.add_argument("--no-pdl", action="store_true",
                      help="launch without programmatic dependent launch (default: with, WT_LAUNCH_PDL)")
     ap_.add_argument("--layers", type=int, default=32,
@@ -628,8 +830,8 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+        if rank == 0:  # (the other ranks of a torchrun launch exit without work)
+            print(json.dumps(run_reference(args, world)), flush=True)
         return
 
     import torch
@@ -647,18 +849,27 @@ def main() -> None:
 
         _lib.set_launch_flags(_lib.WT_LAUNCH_PDL)
     res = run_ours(args, rank, world, local_rank)
-    if world == 1 and args.also:
-        also_args = argparse.Namespace(**{**vars(args), "workload": args.also})
+    also = [w for w in args.also.split(",") if w and w != args.workload]
+    if also:
+        res["also"] = {}
+    for name in also:  # (every rank runs the same workloads in the same order: the same collectives)
         torch.cuda.empty_cache()
-        a = run_ours(also_args, rank, world, local_rank)
-        res["also"] = {args.also: {k: a[k] for k in ("value", "unit", "ms_per_step", "us_per_step",
-                                                       "frac_of_hbm_peak")}
-                       | {"workload": a["config"]["workload"], "roofline_frac": a["roofline"]["frac"],
-                          "bytes_per_step": a["config"]["bytes_per_step"]}}
+        a = run_ours(argparse.Namespace(**{**vars(args), "workload": name}), rank, world, local_rank, light=True)
+        res["also"][name] = {k: a[k] for k in ("value", "unit", "ms_per_step", "us_per_step", "rows_steps_per_s",
+                                               "frac_of_hbm_peak", "clocks")} | {
+            "workload": a["config"]["workload"], "mean_cached_positions": a["config"]["mean_cached_positions"],
+            "bytes_per_step": a["config"]["bytes_per_step"], "roofline_frac": a["roofline"]["frac"],
+            "self_attn_frac": a["roofline"]["self_attn"]["frac"]}
+        if "bytes_per_step_logical" in a["config"]:
+            res["also"][name]["bytes_per_step_logical"] = a["config"]["bytes_per_step_logical"]
+            res["also"][name]["bytes"] = a["config"]["bytes"]
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_ref_gpu:
+        res["vs_reference_gpu"] = run_reference_gpu(local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         wl = WORKLOADS[args.workload]
-        res["cpu_baseline"] = run_cpu_baseline(wl, Schedule(wl, args.warmup + args.steps + 4, 1234, start=args.warmup),
-                                               args.cpu_seconds,
+        res["cpu_baseline"] = run_cpu_baseline(wl, Schedule(wl, args.warmup + args.steps + 4, shard_seed(0),
+                                                            start=args.warmup), args.cpu_seconds,
                                                min(wl["windows"], 2))
     elif rank == 0:
         res["cpu_baseline"] = {"value": None, "note": "timed on rank 0 at N=1 only"}

@@ -156,6 +156,7 @@ def test_teacher_forced_beam_candidates_identical(model, ref_ops):
     best 2K candidates drive the (shared) bookkeeping through wt_beam_update, and each step's best-K candidate sets
     must agree (where they do not, the report gives the reference's own gap between the candidates that swapped)."""
     dec, cross = model
+    ref_self_attn_append, ref_cross_attn = ref_ops
     B, K, T = 2, 5, 24
     P, cap = len(PROMPT), len(PROMPT) + T + 2
     V = dec.shape.vocab

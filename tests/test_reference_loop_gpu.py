@@ -57,12 +57,20 @@ def ref():
 
 @pytest.fixture(scope="module")
 def model(ref):
-    """The reference's WhisperModel at whisper-large-v3's shape, its own random initialisation (seed 0), fp16 on the
-    GPU, and every layer's cross-attention keys/values of WINDOWS windows from its encoder on seeded features."""
+    """The reference's WhisperModel at whisper-large-v3's shape on the GPU (fp16), and every layer's cross-attention
+    keys/values of WINDOWS windows from its encoder on seeded features. The decoder's weights, biases and embeddings
+    are re-drawn N(0, 0.02) (seed 0; LayerNorms as constructed), the weight scale the benchmark configs state: with
+    the module's default initialisation the tied N(0, 1) token embedding dominates the residual stream and the
+    decoder repeats its input token by a margin of ~300 logits, which no attention error could change."""
     cfg = ref.config.WhisperConfig(**LARGE_V3)
     torch.manual_seed(0)
     with torch.device("cuda"):
         m = ref.modeling.WhisperModel(cfg)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    with torch.no_grad():
+        for name, p in m.decoder.named_parameters():
+            if "layer_norm" not in name:
+                p.copy_(torch.randn(p.shape, generator=g, device="cuda") * 0.02)
     m = m.half().eval().requires_grad_(False)
     g = torch.Generator(device="cuda").manual_seed(1)
     feats = torch.randn(WINDOWS, cfg.n_mels, 3000, generator=g, device="cuda")
@@ -126,6 +134,7 @@ def _lockstep(ref, cfg, model, cross, mode, rows, gemm, fused, steps):
     names = INT_STATE + (BEAM_STATE if mode == "beam" else ())
     floats = FLOAT_STATE + (("h_score",) if mode == "beam" else ())
     mismatches, worst_logit, worst_float, min_margin, chosen = [], 0.0, 0.0, float("inf"), []
+    # (scores are sums of fp32 log-probabilities: compared relative to their size)
     for step in range(steps):
         theirs._run_step()
         ours._run_step()
@@ -141,7 +150,7 @@ def _lockstep(ref, cfg, model, cross, mode, rows, gemm, fused, steps):
             if not torch.equal(fin, torch.isfinite(y)):
                 differ.append(n)
             elif bool(fin.any()):
-                worst_float = max(worst_float, float((x[fin] - y[fin]).abs().max()))
+                worst_float = max(worst_float, float(((x[fin] - y[fin]).abs() / (1 + x[fin].abs())).max()))
         if differ:
             mismatches.append((step, differ))
         chosen.append(theirs.tokens[:, 0].clone())
@@ -152,11 +161,12 @@ def _lockstep(ref, cfg, model, cross, mode, rows, gemm, fused, steps):
     distinct = len(set(torch.stack(chosen[len(PROMPT) - 1:]).flatten().tolist()))
     report = (f"{mode} x{rows}, gemm {gemm}, fused bookkeeping {fused}: {len(chosen)} steps, "
               f"{len(mismatches)} with a difference {mismatches[:5]}; max |logit diff| {worst_logit:.2e}, "
-              f"max score / no-speech diff {worst_float:.2e}, min top-1 margin {min_margin:.3f}, "
+              f"max score / no-speech diff {worst_float:.2e} (relative to 1 + |score|), min top-1 margin "
+              f"{min_margin:.3e}, "
               f"{distinct} distinct tokens chosen")
     print(report)
     assert not mismatches, report
-    assert worst_float < 0.05, report
+    assert worst_float < 1e-2, report
     assert distinct > 1, report  # (the tokens depend on the windows: the attention is doing something)
     return report
 
@@ -198,7 +208,7 @@ def test_beam_stream_free_running_identical(ref, model):
         scores = [r.hypothesis.score for r in out]
         results[side + "_scores"] = scores
     assert results["ours"] == results["theirs"]
-    diff = max(abs(a - b) for a, b in zip(results["ours_scores"], results["theirs_scores"]))
-    assert diff < 0.05, diff
+    diff = max(abs(a - b) / (1 + abs(b)) for a, b in zip(results["ours_scores"], results["theirs_scores"]))
+    assert diff < 1e-2, diff
     print(f"stream: {WINDOWS} windows, lengths {[r[1] for r in results['ours']]}, identical hypotheses; "
           f"max |score diff| {diff:.2e}")
