@@ -61,6 +61,20 @@ const char *wt_last_error(void);
 /* Process-wide launch flags (WT_LAUNCH_*); returns the previous value. Default: 0. */
 int wt_set_launch_flags(int flags);
 
+/* Bounded waits. Every wait inside a kernel (an mbarrier that a TMA copy or the tensor cores complete, a request
+ * one warp hands another) polls at most this many times, with back-off, then records an error code in the call's
+ * device error word (the first 4 bytes of its workspace / error buffer) and gives up: the kernel returns, its
+ * results are not valid, and the context stays usable. Process-wide, read at each launch; 0 restores the default
+ * (2^22 polls: far beyond any wait that completes); returns the previous value. No counterpart in the reference
+ * (whose kernels have no device-side waits). */
+unsigned wt_set_wait_limit(unsigned polls);
+/* Test hook for the bounded waits: when nonzero, launches of the fused cross-attention (wt_cross_attn) issue no
+ * copy for the first ring stage of their first streaming warp, so that warp's wait on it must run out (after
+ * wt_set_wait_limit's polls) and the call's error word is set; no other copy is affected and nothing is left in
+ * flight. For tests of the failure path only: 0 (the default) in use. Returns the previous value. No counterpart in
+ * the reference. */
+int wt_set_test_withhold_stage(int on);
+
 /* ---------------------------------------------------------------------------------------------------------
  * Self-attention of one new token per row over the row's cache slots < offset[r], each read from the row
  * src[r, j] names, plus the new token itself.

@@ -11,6 +11,9 @@ namespace wt {
 namespace {
 thread_local char g_last_error[512] = "";
 std::atomic<int> g_launch_flags{0};
+constexpr unsigned kDefaultWaitLimit = 1u << 22;
+std::atomic<unsigned> g_wait_limit{kDefaultWaitLimit};
+std::atomic<int> g_withhold_stage{0};
 }  // namespace
 
 int fail(int status, const char *fmt, ...) {
@@ -22,6 +25,8 @@ int fail(int status, const char *fmt, ...) {
 }
 
 int launch_flags() { return g_launch_flags.load(std::memory_order_relaxed); }
+unsigned wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
+int test_withhold_stage() { return g_withhold_stage.load(std::memory_order_relaxed); }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -73,5 +78,11 @@ const char *wt_status_string(int status) {
 const char *wt_last_error(void) { return wt::g_last_error; }
 
 int wt_set_launch_flags(int flags) { return wt::g_launch_flags.exchange(flags); }
+
+unsigned wt_set_wait_limit(unsigned polls) {
+  return wt::g_wait_limit.exchange(polls == 0 ? wt::kDefaultWaitLimit : polls);
+}
+
+int wt_set_test_withhold_stage(int on) { return wt::g_withhold_stage.exchange(on != 0 ? 1 : 0); }
 
 }  // extern "C"

@@ -18,6 +18,8 @@ namespace wt {
 int fail(int status, const char *fmt, ...);  // records the calling thread's message, returns status
 int launch_flags();
 bool aligned16(const void *p);
+unsigned wait_limit();     // polls of every bounded device wait (wt_set_wait_limit)
+int test_withhold_stage();  // the bounded-wait test hook (wt_set_test_withhold_stage)
 
 // ---- per-device queries and settings (thread safe) -------------------------------------------------------
 constexpr int kMaxDevices = 64;

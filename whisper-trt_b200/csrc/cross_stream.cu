@@ -65,6 +65,8 @@ struct StreamArgs {
   long long per_warp;
   int max_slots;
   float scale;
+  uint32_t polls;  // bound of every wait (wt_set_wait_limit)
+  int withhold;    // test hook: no copy for the first stage of warp 0 of CTA 0 (wt_set_test_withhold_stage)
 };
 
 __host__ __device__ inline long long first_warp(long long u, int bpu, long long per_warp) {
@@ -260,7 +262,7 @@ template <typename T, int NT, int kStreamWarps>
 __device__ void serve_requests(const StreamArgs &a, uint64_t *req_bar, const long long *req_u, const int *req_n,
                                int lane) {
   bool waiting = lane < kStreamWarps;
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
+  for (uint32_t it = 0; it < a.polls; ++it) {
     long long u = -1;
     bool completed = false;
     if (waiting && mbar_try_wait(&req_bar[lane], 0)) {
@@ -323,13 +325,17 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   int i_wh = static_cast<int>(u0 / a.QG), i_qg = static_cast<int>(u0 % a.QG);
   int i_b = static_cast<int>(beg - u0 * a.bpu);
   int issued = 0;
+  // (the bounded-wait test hook: warp 0 of CTA 0 issues nothing for its first stage, whose wait then runs out)
+  const bool withhold = a.withhold && gw == 0;
   auto issue_next = [&]() {  // lane 0: the next block of the range into its stage
     const int s = issued % kStreamStages;
     unsigned char *dst = ring + s * kStageBytes;
     const int row = i_wh * a.Tn + i_b * 16;
-    mbar_arrive_expect_tx(&bars[s], kStageBytes);
-    tma_load_2d(dst, &kmap, 0, row, &bars[s]);
-    tma_load_2d(dst + kTileBytes, &vmap, 0, row, &bars[s]);
+    if (!(withhold && issued == 0)) {
+      mbar_arrive_expect_tx(&bars[s], kStageBytes);
+      tma_load_2d(dst, &kmap, 0, row, &bars[s]);
+      tma_load_2d(dst + kTileBytes, &vmap, 0, row, &bars[s]);
+    }
     ++issued;
     if (++i_b == a.bpu) {
       i_b = 0;
@@ -410,7 +416,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
     // two blocks at once when the range's next block belongs to the same (window, head)
     const bool pair = kPair && j + 1 < n && c_b + 1 < a.bpu;
     const int s0 = j % kStreamStages;
-    if (!mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kStreamStages) & 1), a.err, kErrTimeout))
+    if (!mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kStreamStages) & 1), a.err, kErrTimeout, a.polls))
       late |= 1u << s0;
     uint32_t ka[4][4], va[4][4];
     smem_frags(ka, va, ring + s0 * kStageBytes, ring + s0 * kStageBytes + kTileBytes, lane);
@@ -418,7 +424,8 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
     const int used = pair ? 2 : 1;
     if (pair) {
       const int s1 = (j + 1) % kStreamStages;
-      if (!mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kStreamStages) & 1), a.err, kErrTimeout))
+      if (!mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kStreamStages) & 1), a.err, kErrTimeout,
+                             a.polls))
         late |= 1u << s1;
       uint32_t kb[4][4], vb[4][4];
       smem_frags(kb, vb, ring + s1 * kStageBytes, ring + s1 * kStageBytes + kTileBytes, lane);
@@ -463,7 +470,8 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
   for (int j = n - min(n, kStreamStages); j < n; ++j) {
     const int s = j % kStreamStages;
-    if (late & (1u << s)) mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kStreamStages) & 1), nullptr, 0);
+    if (late & (1u << s))
+      mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kStreamStages) & 1), nullptr, 0, a.polls);
   }
 }
 
@@ -567,7 +575,7 @@ int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y
   char *ws = static_cast<char *>(workspace);
   StreamArgs a{q,       y,    reinterpret_cast<float *>(ws + p.part_off), reinterpret_cast<int *>(ws + p.counters_off),
                reinterpret_cast<int *>(ws), W, S, H, Tn, p.qgs, p.bpu, p.total, p.per_warp, p.max_slots,
-               static_cast<float>(1.0 / 8.0 * 1.4426950408889634)};
+               static_cast<float>(1.0 / 8.0 * 1.4426950408889634), wait_limit(), test_withhold_stage()};
   const bool bf = dtype == WT_BF16;
   const int g = p.grid, sh = p.shape;
   switch (p.nt) {

@@ -61,6 +61,7 @@ struct DlArgs {
   const void *res;   // [N, V] (residual mode)
   void *y;           // [N, V]
   int N, V, kblocks, splits, kb_per, vtiles, nmma, tcols, stages, ring_bytes, res_bytes;
+  uint32_t polls;  // bound of every wait (wt_set_wait_limit)
 };
 
 // nmma: the rows of a unit (a row chunk; the MMA's N, a multiple of 16). res_bytes: a region after the ring that
@@ -284,7 +285,7 @@ __global__ void __launch_bounds__(kDlThreads)
               tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
             waited = true;
           }
-          mbar_wait_bounded(&empty[s], ((i / stages) - 1) & 1, a.err, kDlErrTimeout);
+          mbar_wait_bounded(&empty[s], ((i / stages) - 1) & 1, a.err, kDlErrTimeout, a.polls);
         }
         unsigned char *st = smem + s * stage_bytes;
         mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(a_bytes + b_bytes));
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(kDlThreads)
       const uint32_t idesc = idesc_f16(kDlTileV, a.nmma, kBF16);
       for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
-        mbar_wait_bounded(&full[s], (i / stages) & 1, a.err, kDlErrTimeout);
+        mbar_wait_bounded(&full[s], (i / stages) & 1, a.err, kDlErrTimeout, a.polls);
         tc_fence_after();
         const uint32_t a_addr = smem_addr(smem + s * stage_bytes), b_addr = a_addr + a_bytes;
         const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(b_addr);
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(kDlThreads)
         }
       }
     }
-    mbar_wait_bounded(&acc_full[0], 0, a.err, kDlErrTimeout);
+    mbar_wait_bounded(&acc_full[0], 0, a.err, kDlErrTimeout, a.polls);
     tc_fence_after();
     const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     T *y = static_cast<T *>(a.y);
@@ -652,7 +653,7 @@ int launch_gemm(int dtype, const void *x, const void *w, const void *b, const vo
   st = encode_tile_map(&xm, x, static_cast<unsigned long long>(N), static_cast<unsigned long long>(K), p.nmma, dtype);
   if (st != WT_OK) return st;
   DlArgs a{reinterpret_cast<int *>(workspace), b, res, y, N, V, p.kblocks, p.splits, p.kb_per, p.vtiles, p.nmma,
-           p.tcols, p.stages, p.ring_bytes, p.res_bytes};
+           p.tcols, p.stages, p.ring_bytes, p.res_bytes, wait_limit()};
   return launch_clustered("dec_linear", kernel, dim3(p.grid), dim3(kDlThreads), p.smem, stream, p.splits, wm, xm, a);
 }
 

@@ -35,7 +35,8 @@ constexpr int kLgErrTimeout = 1;
 template <bool BF16>
 __global__ void __launch_bounds__(kLgThreads)
     logits_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                  float *__restrict__ y, int N, int V, int kblocks, int nmma, int tcols, int stages, int *err) {
+                  float *__restrict__ y, int N, int V, int kblocks, int nmma, int tcols, int stages, int *err,
+                  uint32_t polls) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(kLgThreads)
         const int v0 = (t % vtiles) * kLgTileV, n0 = (t / vtiles) * kLgMaxRows;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % stages;
-          if (it >= stages) mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1, err, kLgErrTimeout);
+          if (it >= stages) mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1, err, kLgErrTimeout, polls);
           unsigned char *st = smem + s * stage_bytes;
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(a_bytes + b_bytes));
           tma_load_2d(st, &wmap, kb * kLgKBlock, v0, &full[s]);
@@ -96,12 +97,12 @@ __global__ void __launch_bounds__(kLgThreads)
       int it = 0, j = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
         const int b = j & 1;
-        if (j >= 2) mbar_wait_bounded(&acc_empty[b], ((j >> 1) - 1) & 1, err, kLgErrTimeout);
+        if (j >= 2) mbar_wait_bounded(&acc_empty[b], ((j >> 1) - 1) & 1, err, kLgErrTimeout, polls);
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(b * tcols);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % stages;
-          mbar_wait_bounded(&full[s], (it / stages) & 1, err, kLgErrTimeout);
+          mbar_wait_bounded(&full[s], (it / stages) & 1, err, kLgErrTimeout, polls);
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + s * stage_bytes), b_addr = a_addr + a_bytes;
           const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(b_addr);
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kLgThreads)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int b = j & 1;
       const int v = (t % vtiles) * kLgTileV + quarter * 32 + lane, n0 = (t / vtiles) * kLgMaxRows;
-      mbar_wait_bounded(&acc_full[b], (j >> 1) & 1, err, kLgErrTimeout);
+      mbar_wait_bounded(&acc_full[b], (j >> 1) & 1, err, kLgErrTimeout, polls);
       tc_fence_after();
       const uint32_t base = tmem + static_cast<uint32_t>(b * tcols) + (static_cast<uint32_t>(quarter * 32) << 16);
       for (int c0 = 0; c0 < nmma; c0 += 16) {
@@ -184,5 +185,5 @@ extern "C" int wt_logits32(int dtype, const void *x, const void *w, float *y, in
   const int tiles = ((vocab + kLgTileV - 1) / kLgTileV) * chunks;
   const int grid = tiles < sms ? tiles : sms;
   return launch("logits32", kernel, dim3(grid), dim3(kLgThreads), smem, stream, wm, xm, y, rows, vocab, kblocks,
-                nmma, tcols, stages, err);
+                nmma, tcols, stages, err, wait_limit());
 }

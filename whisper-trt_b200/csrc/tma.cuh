@@ -57,10 +57,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for phase `parity` of `bar`, giving up after a bounded number of polls (each try_wait itself suspends for a
-// while): on a timeout the kernel records `code` in *err (if given) and returns false -- it never hangs the GPU.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+// Wait for phase `parity` of `bar`, giving up after `limit` polls (each try_wait itself suspends for a while; the
+// host's wt_set_wait_limit, 2^22 by default): on a timeout the kernel records `code` in *err (if given) and returns
+// false -- it never hangs the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code,
+                                                  uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 64) __nanosleep(64);
   }

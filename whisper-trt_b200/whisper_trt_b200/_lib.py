@@ -21,6 +21,8 @@ SIGNATURES = {
     "wt_status_string": (c_char_p, [c_int]),
     "wt_last_error": (c_char_p, []),
     "wt_set_launch_flags": (c_int, [c_int]),
+    "wt_set_wait_limit": (ctypes.c_uint, [ctypes.c_uint]),
+    "wt_set_test_withhold_stage": (c_int, [c_int]),
     "wt_self_attn_step_workspace": (c_size, [c_int, c_int, c_int, c_int]),
     "wt_self_attn_step_splits": (c_int, [c_int, c_int, c_int, c_int]),
     "wt_self_attn_step": (c_int, [c_int, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
