@@ -183,6 +183,30 @@ int wt_beam_update(const float *top_s, const int64_t *top_i, int64_t *t, int64_t
                    int hyp_slots, int prompt_len, int vocab, int eot, void *stream);
 int wt_slot_reset(int32_t *src, const int64_t *slots, int n_slots, int windows, int beams, int capacity,
                   int prefilled, void *stream);
+/* wt_beam_update_mixed: wt_beam_update for a beam search with sampled slots (the reference's
+ *   Search(sampling_slots=True)); replaces beam_kernels.py:169-269 _update_kernel with MIXED (its sampled branch
+ *   :200-225). Windows with sampling[b] != 0 follow CTranslate2's GreedySearch rules on their rows' sampled tokens
+ *   (samp_tok / samp_score [N], from wt_beam_sample): a row not yet done adds its token's log-probability to cum,
+ *   appends the token to its history and length unless it is EOS, is done after EOS or at the last step; every row
+ *   takes its token and marks its new slot; the window is done when all its rows are, else it advances. Other
+ *   windows follow wt_beam_update. row_done [N] 0/1 bytes, length [N] int64. With sampling == NULL it is
+ *   wt_beam_update (the other four may then be NULL). */
+int wt_beam_update_mixed(const float *top_s, const int64_t *top_i, int64_t *t, int64_t *pos, const int64_t *sot_pos,
+                         const float *ns, float *no_speech, uint8_t *done, int64_t *hist, float *cum, int32_t *src,
+                         int64_t *tokens, const int64_t *forced, int64_t *h_count, float *h_score, int64_t *h_len,
+                         int64_t *h_tokens, const int64_t *last_t, const uint8_t *sampling, const int64_t *samp_tok,
+                         const float *samp_score, uint8_t *row_done, int64_t *length, int windows, int beams,
+                         int capacity, int hist_len, int hyp_slots, int prompt_len, int vocab, int eot,
+                         void *stream);
+/* wt_beam_sample: each sampled row's next token, by Gumbel-max -- replaces beam_kernels.py:284-289 sample() (kernel
+ *   :136-167) and the sampling of search.py:342-346 (_greedy), with search.py:104-129 uniform()'s counter-based
+ *   random numbers. For every row r of a window b with sampling[b] != 0, done[b] == 0, t[b] >= 0 and
+ *   row_done[r] == 0: u_v = uniform(seed[b], t[b], r % beams, v), g_v = scores[r, v] / temperature[b]
+ *   - log(-log(max(u_v, 1e-20))); samp_tok[r] = the first v with the largest g_v, samp_score[r] = scores[r, that v]
+ *   (scores [N, V]: the rows' log-probabilities, as wt_beam_scores_mixed writes them). Other rows are untouched. */
+int wt_beam_sample(const float *scores, const int64_t *t, const uint8_t *done, const uint8_t *row_done,
+                   const uint8_t *sampling, const float *temperature, const int64_t *seed, int64_t *samp_tok,
+                   float *samp_score, int windows, int beams, int vocab, void *stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * The vocabulary projection, fp32 accumulate and output: y [N, V] = x [N, d] . w [V, d]^T (x, w fp16 or bf16,
@@ -213,6 +237,14 @@ int wt_beam_scores(const float *logits, const uint8_t *suppress, const uint8_t *
                    float *top_s, int64_t *top_i, int windows, int beams, int vocab, int hist_len, int timestamps,
                    int no_speech, int no_timestamps, int ts_begin, int eot, void *workspace, size_t workspace_bytes,
                    void *stream);
+/* wt_beam_scores_mixed: wt_beam_scores for a search with sampled slots (beam_kernels.py:351-361 with MIXED,
+ *   kernel :105-106): the rows of windows with sampling[b] != 0 score their log-probabilities alone (no cum);
+ *   sampling [B] 0/1 bytes, or NULL (= wt_beam_scores). */
+int wt_beam_scores_mixed(const float *logits, const uint8_t *suppress, const uint8_t *begin, const int64_t *t,
+                         const float *cum, const uint8_t *sampling, const int64_t *hist, const int64_t *max_initial,
+                         float *scores, float *ns, float *top_s, int64_t *top_i, int windows, int beams, int vocab,
+                         int hist_len, int timestamps, int no_speech, int no_timestamps, int ts_begin, int eot,
+                         void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * The decoder step's linear layers with their LayerNorm, bias, GELU and residual fused around them, on the

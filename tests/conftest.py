@@ -46,3 +46,10 @@ def decoder_golden():
     import numpy as np
 
     return np.load(ROOT / "tests" / "golden" / "decoder_golden.npz")
+
+
+@pytest.fixture(scope="session")
+def mixed_golden():
+    import numpy as np
+
+    return np.load(ROOT / "tests" / "golden" / "mixed_golden.npz")

@@ -6,8 +6,9 @@ Run where the reference source tree is importable (it does not travel to the GPU
     python tests/golden/make_golden.py --reference-src <path to the reference's src/ directory>
 
 Writes ``attn_golden.npz`` (attention outputs + input digests), ``slots_golden.npz`` (per-step search states
-before/after the reference's bookkeeping), ``scores_golden.npz`` (beam scoring) and ``decoder_golden.npz`` (the
-fused decoder linear layers; ``--only decoder`` writes just this one) next to this script.
+before/after the reference's bookkeeping), ``scores_golden.npz`` (beam scoring), ``mixed_golden.npz`` (beam search
+with sampled slots; ``--only mixed`` writes just this one) and ``decoder_golden.npz`` (the fused decoder linear
+layers; ``--only decoder`` writes just this one) next to this script.
 """
 
 from __future__ import annotations
@@ -144,6 +145,80 @@ def slots_golden(ref_src: str) -> dict:
     return out
 
 
+# --- beam search with sampled slots (Search(sampling_slots=True)): the reference Search, PyTorch path, CPU ---------
+MIXED_V = 257  # (not a multiple of the sampling kernel's thread count)
+MIXED_FIELDS = STATE_FIELDS + ("row_done", "length", "sampling", "temperature", "seed", "suppress", "begin",
+                               "max_initial")
+
+
+def _mixed_logits(history, seed):
+    g = torch.Generator().manual_seed(zlib.crc32(repr(("mixed-golden", seed, history)).encode()))
+    x = torch.randn(MIXED_V, generator=g, dtype=torch.float64) * 2.0
+    x[EOT] += 0.12 * len(history)
+    return x
+
+
+def mixed_golden(ref_src: str) -> dict:
+    """Per step of the reference's beam search with sampled slots (Search(sampling_slots=True), its PyTorch
+    bookkeeping on CPU: search.py:290-312 _choose, :342-354 _greedy, :367-409 _beam, :104-129 uniform), decoding a
+    stream of windows at temperatures 0 (beam), 0.5 and 1.0 (sampled, some on fewer rows than the slot has, as the
+    reference's test_serve.py:62-72 makes them): the state before the step, the step's logits and the state after."""
+    from whisper_trt.config import WhisperConfig
+    from whisper_trt.search import Job, Search, mix_seed
+
+    cfg = WhisperConfig(n_mels=4, d_model=4, enc_layers=1, enc_heads=1, enc_ffn=4, dec_layers=1, dec_heads=1,
+                        dec_ffn=4, vocab_size=MIXED_V, eot=EOT, sot=SOT, no_speech=NOSPEECH)
+    out = {}
+    step_no = 0
+    for run, (K, seed) in enumerate([(4, 20), (3, 21)]):
+        W = 3
+        jobs = []
+        for w in range(7):
+            temperature = (0.0, 0.5, 1.0)[w % 3]
+            rows = (K if w % 2 else max(1, K - 1)) if temperature > 0 else None
+            jobs.append(Job([SOT, 10 + w, 20 + w % 3, 30], temperature, mix_seed(7, w), rows, key=w))
+        search = Search(cfg, _fake_step_with(_mixed_logits, seed), W, K, 4, "beam", dtype=torch.float32,
+                        device="cpu", max_length=36, graphs=False, fused=False, sampling_slots=True)
+        rec = {}
+        orig_choose, orig_body = search._choose, search._body
+
+        def choose(logits, s=search, orig=orig_choose, rec=rec):
+            rec["logits"] = logits.clone()
+            orig(logits)
+
+        def body(s=search, orig=orig_body, rec=rec):
+            nonlocal step_no
+            before = {f: getattr(s, f).clone() for f in MIXED_FIELDS}
+            orig()
+            key = f"step{step_no:04d}"
+            for f in MIXED_FIELDS:
+                out[f"{key}/before/{f}"] = before[f].numpy()
+                out[f"{key}/after/{f}"] = getattr(s, f).numpy().copy()
+            out[f"{key}/logits"] = rec["logits"].numpy()
+            out[f"{key}/meta"] = np.array([K, s.P, MIXED_V, EOT, NOSPEECH, run], dtype=np.int64)
+            step_no += 1
+
+        search._choose = choose
+        search._body = body
+
+        class Src:
+            def __init__(self, jobs):
+                self.ready = list(jobs)
+
+            def take(self, n, block=False):
+                got, self.ready = self.ready[:n], self.ready[n:]
+                return got
+
+            def load(self, slots, jobs):
+                pass
+
+            def result(self, job, result):
+                pass
+
+        search.serve(Src(jobs), [5, 6, 7], [8, EOT], check_every=1, ahead=1)
+    return out
+
+
 # --- the beam step's candidate scores: masks, timestamp rules, log-softmax + cum, top-2K (reference Search) ------
 TS_V, TS_NOTS, TS_TSB = 120, 40, 41  # toy vocabulary with timestamps: text 4..39, <|notimestamps|> 40, 41.. times
 
@@ -274,9 +349,14 @@ def decoder_golden(ref_src: str) -> dict:
 def main() -> None:
     ap_ = argparse.ArgumentParser()
     ap_.add_argument("--reference-src", required=True)
-    ap_.add_argument("--only", choices=["decoder"], default=None, help="write only this fixture")
+    ap_.add_argument("--only", choices=["decoder", "mixed"], default=None, help="write only this fixture")
     args = ap_.parse_args()
     sys.path.insert(0, args.reference_src)
+    if args.only == "mixed":
+        m = mixed_golden(args.reference_src)
+        np.savez_compressed(HERE / "mixed_golden.npz", **m)
+        print(f"mixed-slot steps: {sum(k.endswith('/meta') for k in m)}")
+        return
     if args.only == "decoder":
         d = decoder_golden(args.reference_src)
         np.savez_compressed(HERE / "decoder_golden.npz", **d)
@@ -293,6 +373,7 @@ def main() -> None:
     sc = scores_golden(args.reference_src)
     np.savez_compressed(HERE / "scores_golden.npz", **sc)
     np.savez_compressed(HERE / "decoder_golden.npz", **decoder_golden(args.reference_src))
+    np.savez_compressed(HERE / "mixed_golden.npz", **mixed_golden(args.reference_src))
     print(f"attn cases: {len(cases.ATTN_CASES)}; bookkeeping steps: {sum(k.endswith('/meta') for k in s)}; "
           f"scoring steps: {sum(k.endswith('/meta') for k in sc)}")
 

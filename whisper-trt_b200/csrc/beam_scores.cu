@@ -219,6 +219,7 @@ struct ScoreArgs {
   const uint8_t *suppress, *begin;
   const int64_t *t, *hist, *max_initial;
   const float *cum;
+  const uint8_t *sampling;  // [B] or null: a sampled window's rows score without their cumulative log-probability
   float *scores, *ns, *top_s;
   int64_t *top_i;
   float *row_s;  // workspace: [N, kk] row lists
@@ -427,7 +428,7 @@ __global__ void __launch_bounds__(kScoreThreads, 4) beam_scores_kernel(const Sco
       log_sum = logf(tss.s);
     }
   }
-  const float c = a.cum[r];
+  const float c = (a.sampling != nullptr && a.sampling[b] != 0) ? 0.f : a.cum[r];
   const int cand0 = (r - b * K) * V;
   if (r == b * K && rank == 0 && tid == 0) a.ns[b] = expf(x[a.no_speech] - (m_raw + logf(s_raw)));
 
@@ -821,6 +822,16 @@ int wt_beam_scores(const float *logits, const uint8_t *suppress, const uint8_t *
                    float *top_s, int64_t *top_i, int windows, int beams, int vocab, int hist_len, int timestamps,
                    int no_speech, int no_timestamps, int ts_begin, int eot, void *workspace, size_t workspace_bytes,
                    void *stream) {
+  return wt_beam_scores_mixed(logits, suppress, begin, t, cum, nullptr, hist, max_initial, scores, ns, top_s, top_i,
+                              windows, beams, vocab, hist_len, timestamps, no_speech, no_timestamps, ts_begin, eot,
+                              workspace, workspace_bytes, stream);
+}
+
+int wt_beam_scores_mixed(const float *logits, const uint8_t *suppress, const uint8_t *begin, const int64_t *t,
+                         const float *cum, const uint8_t *sampling, const int64_t *hist, const int64_t *max_initial,
+                         float *scores, float *ns, float *top_s, int64_t *top_i, int windows, int beams, int vocab,
+                         int hist_len, int timestamps, int no_speech, int no_timestamps, int ts_begin, int eot,
+                         void *workspace, size_t workspace_bytes, void *stream) {
   using namespace wt;
   WT_REQUIRE(windows > 0 && beams > 0 && vocab > 0 && hist_len > 0, WT_ERR_ARG,
              "beam_scores: sizes must be positive (windows %d, beams %d, vocab %d, hist_len %d)", windows, beams,
@@ -846,7 +857,7 @@ int wt_beam_scores(const float *logits, const uint8_t *suppress, const uint8_t *
   const int per_cta = (vocab + kScoreCluster - 1) / kScoreCluster;
   const int cap = kk * max(kScoreWarps, (per_cta + kScoreThreads - 1) / kScoreThreads) + 64;
   WT_REQUIRE(cap * 8 <= 160 * 1024, WT_ERR_UNSUPPORTED, "beam_scores: vocabulary %d too large", vocab);
-  ScoreArgs a{logits, suppress, begin, t, hist, max_initial, cum, scores, ns, top_s, top_i,
+  ScoreArgs a{logits, suppress, begin, t, hist, max_initial, cum, sampling, scores, ns, top_s, top_i,
               reinterpret_cast<float *>(ws + counters), reinterpret_cast<int *>(ws + counters + lists_s),
               reinterpret_cast<int *>(ws), beams, vocab, hist_len, kk, cap, timestamps, no_speech, no_timestamps,
               ts_begin, eot};

@@ -115,6 +115,13 @@ struct UpdateArgs {
   float *h_score;
   int64_t *h_len, *h_tokens;
   const int64_t *last_t;
+  // sampled slots (all null when the search has none, as wt_beam_update passes): per window whether it is sampled,
+  // per row its sampled token and that token's log-probability (wt_beam_sample), whether it is done, its length
+  const uint8_t *sampling;
+  const int64_t *samp_tok;
+  const float *samp_score;
+  uint8_t *row_done;
+  int64_t *length;
   int K, C, T, S, P, V, eot;
 };
 
@@ -126,8 +133,9 @@ template <int KMAX>
 __global__ void __launch_bounds__(128) beam_update_kernel(UpdateArgs a) {
   const int b = blockIdx.x, tid = threadIdx.x;
   const int K = a.K, C = a.C, T = a.T;
-  __shared__ int s_mode;  // 0: untouched, 1: prompt token, 2: beam step
+  __shared__ int s_mode;  // 0: untouched, 1: prompt token, 2: beam step, 3: sampled step
   __shared__ int64_t s_tb, s_pb;
+  __shared__ int s_live_rows;
   __shared__ int s_par[KMAX], s_newpar[KMAX], s_slot[KMAX];
   __shared__ int64_t s_tok[KMAX], s_newtok[KMAX];
   __shared__ float s_ps[KMAX], s_news[KMAX];
@@ -140,7 +148,9 @@ __global__ void __launch_bounds__(128) beam_update_kernel(UpdateArgs a) {
     s_tb = tb;
     s_pb = pb;
     if (pb == a.sot_pos[b]) a.no_speech[b] = a.ns[b];
-    s_mode = tb < 0 ? 1 : (db ? 0 : 2);
+    const bool sampled = a.sampling != nullptr && a.sampling[b] != 0;
+    s_mode = tb < 0 ? 1 : (db ? 0 : (sampled ? 3 : 2));
+    s_live_rows = 0;
     if (s_mode == 2) {
       const int64_t *ti = a.top_i + static_cast<size_t>(b) * 2 * K;
       const float *ts = a.top_s + static_cast<size_t>(b) * 2 * K;
@@ -211,6 +221,34 @@ __global__ void __launch_bounds__(128) beam_update_kernel(UpdateArgs a) {
     }
     return;
   }
+  if (mode == 3) {  // a sampled window: GreedySearch's rules on each row's own sampled token (beam_kernels.py:200-225)
+    if (tid < K) {
+      const int r = b * K + tid;
+      const int64_t tok = a.samp_tok[r];
+      bool rd = a.row_done[r] != 0;
+      if (!rd) a.cum[r] = a.cum[r] + a.samp_score[r];
+      const bool eos = tok == a.eot, last = tb == a.last_t[b];
+      if (!rd && !eos) {  // a generated token (EOS is not part of the hypothesis)
+        if (tb >= 0 && tb < T) a.hist[static_cast<size_t>(r) * T + tb] = tok;
+        a.length[r] += 1;
+      }
+      rd = rd || eos || last;
+      a.row_done[r] = rd;
+      a.tokens[r] = tok;
+      if (pb >= 0 && pb < C) a.src[static_cast<size_t>(r) * C + pb] = r;  // the row's own new slot
+      if (!rd) atomicAdd(&s_live_rows, 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const bool ended = s_live_rows == 0;
+      a.done[b] = ended;
+      if (!ended) {
+        a.pos[b] = pb + 1;
+        a.t[b] = tb + 1;
+      }
+    }
+    return;
+  }
   // beam step: every read of the window's rows before any write, column by column per thread
   for (int cc = tid; cc < C; cc += blockDim.x) {
     int32_t vals[KMAX];
@@ -254,6 +292,84 @@ __global__ void __launch_bounds__(128) beam_update_kernel(UpdateArgs a) {
       a.pos[b] = pb + 1;
       a.t[b] = tb + 1;
     }
+  }
+}
+
+// ---- sampled slots: each sampled row's token by Gumbel-max (beam_kernels.py:136-167; search.py:104-129,342-346) -----
+// The reference's counter-based uniform (search.uniform): a 32-bit counter of (seed, step, row within the window,
+// token) through PCG's output permutation twice, in 64-bit integer arithmetic masked to 32 bits, then
+// (float(x) + 0.5) / 2^32 -- a function of the window's seed and step only, so a window draws the same numbers in any
+// slot and inside a CUDA graph (no generator state).
+__device__ __forceinline__ float counter_uniform(int64_t x) {
+  constexpr uint64_t m = 0xFFFFFFFFull;
+  uint64_t v = static_cast<uint64_t>(x) & m;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    v = (v * 747796405ull + 2891336453ull) & m;
+    v = (((v >> ((v >> 28) + 4)) ^ v) * 277803737ull) & m;
+    v = ((v >> 22) ^ v) & m;
+  }
+  return (__ull2float_rn(v) + 0.5f) * (1.0f / 4294967296.0f);
+}
+
+struct SampleArgs {
+  const float *scores;  // [N, V]: log-probabilities of the sampled rows (wt_beam_scores_mixed)
+  const int64_t *t;
+  const uint8_t *done, *row_done, *sampling;
+  const float *temperature;
+  const int64_t *seed;
+  int64_t *samp_tok;
+  float *samp_score;
+  int K, V;
+};
+
+constexpr int kSampleThreads = 256;
+
+// One CTA per row: g = score / temperature - log(-log(max(u, 1e-20))) over the vocabulary, its first maximum.
+__global__ void __launch_bounds__(kSampleThreads) beam_sample_kernel(SampleArgs a) {
+  const int r = blockIdx.x, b = r / a.K, tid = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t tw = a.t[b];
+  if (!(a.sampling[b] != 0 && a.done[b] == 0 && tw >= 0 && a.row_done[r] == 0)) return;  // (the whole CTA)
+  const float temp = a.temperature[b];
+  const int64_t mix = a.seed[b] * 0x6C8E9CF5LL + tw * 0x85EBCA77LL + static_cast<int64_t>(r % a.K) * a.V;
+  const float *x = a.scores + static_cast<size_t>(r) * a.V;
+  float best = kNegInf;
+  int bi = a.V;
+  for (int v = tid; v < a.V; v += kSampleThreads) {  // (ascending per thread: a strict > keeps the first maximum)
+    const float u = fmaxf(counter_uniform(mix + v), 1e-20f);
+    const float g = __fdiv_rn(x[v], temp) - logf(-logf(u));
+    if (g > best) {
+      best = g;
+      bi = v;
+    }
+  }
+  __shared__ float s_best[kSampleThreads / 32];
+  __shared__ int s_bi[kSampleThreads / 32];
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if ((tid & 31) == 0) {
+    s_best[tid >> 5] = best;
+    s_bi[tid >> 5] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < kSampleThreads / 32; ++w)
+      if (s_best[w] > best || (s_best[w] == best && s_bi[w] < bi)) {
+        best = s_best[w];
+        bi = s_bi[w];
+      }
+    if (bi >= a.V) bi = 0;  // (no candidate compared greater than -inf: the reference keeps index 0)
+    a.samp_tok[r] = bi;
+    a.samp_score[r] = x[bi];
   }
 }
 
@@ -340,7 +456,21 @@ int wt_beam_update(const float *top_s, const int64_t *top_i, int64_t *t, int64_t
                    int64_t *tokens, const int64_t *forced, int64_t *h_count, float *h_score, int64_t *h_len,
                    int64_t *h_tokens, const int64_t *last_t, int windows, int beams, int capacity, int hist_len,
                    int hyp_slots, int prompt_len, int vocab, int eot, void *stream) {
+  return wt_beam_update_mixed(top_s, top_i, t, pos, sot_pos, ns, no_speech, done, hist, cum, src, tokens, forced,
+                              h_count, h_score, h_len, h_tokens, last_t, nullptr, nullptr, nullptr, nullptr, nullptr,
+                              windows, beams, capacity, hist_len, hyp_slots, prompt_len, vocab, eot, stream);
+}
+
+int wt_beam_update_mixed(const float *top_s, const int64_t *top_i, int64_t *t, int64_t *pos, const int64_t *sot_pos,
+                         const float *ns, float *no_speech, uint8_t *done, int64_t *hist, float *cum, int32_t *src,
+                         int64_t *tokens, const int64_t *forced, int64_t *h_count, float *h_score, int64_t *h_len,
+                         int64_t *h_tokens, const int64_t *last_t, const uint8_t *sampling, const int64_t *samp_tok,
+                         const float *samp_score, uint8_t *row_done, int64_t *length, int windows, int beams,
+                         int capacity, int hist_len, int hyp_slots, int prompt_len, int vocab, int eot,
+                         void *stream) {
   using namespace wt;
+  WT_REQUIRE(sampling == nullptr || (samp_tok && samp_score && row_done && length), WT_ERR_ARG,
+             "beam_update: sampled slots need samp_tok, samp_score, row_done and length");
   WT_REQUIRE(windows > 0 && beams > 0 && capacity > 0 && hist_len > 0 && vocab > 0 && prompt_len >= 1, WT_ERR_ARG,
              "beam_update: sizes must be positive");
   WT_REQUIRE(beams <= kMaxBeams, WT_ERR_UNSUPPORTED, "beam_update: at most %d beams", kMaxBeams);
@@ -349,10 +479,23 @@ int wt_beam_update(const float *top_s, const int64_t *top_i, int64_t *t, int64_t
                  forced && h_count && h_score && h_len && h_tokens && last_t,
              WT_ERR_ARG, "beam_update: null pointer");
   UpdateArgs a{top_s, top_i, t, pos, sot_pos, ns, no_speech, done, hist, cum, src, tokens, forced, h_count,
-               h_score, h_len, h_tokens, last_t, beams, capacity, hist_len, hyp_slots, prompt_len, vocab, eot};
+               h_score, h_len, h_tokens, last_t, sampling, samp_tok, samp_score, row_done, length, beams, capacity,
+               hist_len, hyp_slots, prompt_len, vocab, eot};
   const dim3 grid(windows), block(128);
   if (beams <= 8) return launch("beam_update", beam_update_kernel<8>, grid, block, 0, stream, a);
   return launch("beam_update", beam_update_kernel<32>, grid, block, 0, stream, a);
+}
+
+int wt_beam_sample(const float *scores, const int64_t *t, const uint8_t *done, const uint8_t *row_done,
+                   const uint8_t *sampling, const float *temperature, const int64_t *seed, int64_t *samp_tok,
+                   float *samp_score, int windows, int beams, int vocab, void *stream) {
+  using namespace wt;
+  WT_REQUIRE(windows > 0 && beams > 0 && vocab > 0, WT_ERR_ARG, "beam_sample: sizes must be positive");
+  WT_REQUIRE(static_cast<long long>(windows) * beams < (1LL << 31), WT_ERR_ARG, "beam_sample: too many rows");
+  WT_REQUIRE(scores && t && done && row_done && sampling && temperature && seed && samp_tok && samp_score,
+             WT_ERR_ARG, "beam_sample: null pointer");
+  SampleArgs a{scores, t, done, row_done, sampling, temperature, seed, samp_tok, samp_score, beams, vocab};
+  return launch("beam_sample", beam_sample_kernel, dim3(windows * beams), dim3(kSampleThreads), 0, stream, a);
 }
 
 int wt_slot_reset(int32_t *src, const int64_t *slots, int n_slots, int windows, int beams, int capacity,

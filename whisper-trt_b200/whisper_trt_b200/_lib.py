@@ -43,9 +43,12 @@ SIGNATURES = {
                                 c_int, c_int, c_void]),
     "wt_beam_update": (c_int, [c_void] * 18 + [c_int] * 8 + [c_void]),
     "wt_slot_reset": (c_int, [c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void]),
+    "wt_beam_update_mixed": (c_int, [c_void] * 23 + [c_int] * 8 + [c_void]),
+    "wt_beam_sample": (c_int, [c_void] * 9 + [c_int] * 3 + [c_void]),
     "wt_logits32": (c_int, [c_int, c_void, c_void, c_void, c_int, c_int, c_int, c_void, c_void]),
     "wt_beam_scores_workspace": (c_size, [c_int, c_int]),
     "wt_beam_scores": (c_int, [c_void] * 11 + [c_int] * 9 + [c_void, c_size, c_void]),
+    "wt_beam_scores_mixed": (c_int, [c_void] * 12 + [c_int] * 9 + [c_void, c_size, c_void]),
     "wt_dec_linear_workspace": (c_size, [c_int, c_int, c_int, c_int]),
     "wt_layer_norm_bias": (c_int, [c_int, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_float, c_void]),
     "wt_ln_linear": (c_int, [c_int] + [c_void] * 6 + [c_int] * 4 + [c_float, c_void, c_size, c_void]),

@@ -14,7 +14,10 @@ kernels (``wt_beam_reorder``, ``wt_beam_update``, ``wt_slot_reset``); integer wo
   candidates in one kernel (``wt_beam_scores``): the reference's beam_kernels.scores (beam_kernels.py:351-361,
   kernel :36-135) and the torch.topk after it (search.py:253);
 * :func:`step_bookkeeping` -- scores, best 2K and update: the fused branch of the reference's Search._body
-  (search.py:251-256) in two kernels.
+  (search.py:251-256) in two kernels;
+* :func:`sample` -- sampled slots (Search(sampling_slots=True)): each sampled row's token by Gumbel-max with the
+  reference's counter-based random numbers (beam_kernels.py:136-167, search.py:104-129), which :func:`update` then
+  applies under CTranslate2's GreedySearch rules.
 """
 
 from __future__ import annotations
@@ -92,11 +95,12 @@ def beam_reorder(src: torch.Tensor, parent: torch.Tensor, pos: torch.Tensor, his
 
 
 def update(s, top_s: torch.Tensor, top_i: torch.Tensor, ns: torch.Tensor) -> None:
-    """The step's bookkeeping on ``s`` (a search state with the reference Search's buffers, beam mode, no sampled
-    slots) from the best 2K candidates -- the reference's beam_kernels.update (beam_kernels.py:292-302)."""
+    """The step's bookkeeping on ``s`` (a search state with the reference Search's buffers, beam mode) from the best
+    2K candidates -- the reference's beam_kernels.update (beam_kernels.py:292-302). With sampled slots
+    (``s.mixed``, Search(sampling_slots=True)) the sampled windows take their rows' tokens from :func:`sample`
+    (``s.samp_tok``, ``s.samp_score``) under CTranslate2's GreedySearch rules."""
     what = "beam_update"
-    if getattr(s, "mixed", False):
-        raise ValueError(f"{what}: sampled slots (sampling_slots=True) are not supported by this kernel")
+    mixed = bool(getattr(s, "mixed", False))
     B, K = s.pos.shape[0], s.K
     n, c = s.src.shape
     T = s.hist.shape[1]
@@ -110,14 +114,48 @@ def update(s, top_s: torch.Tensor, top_i: torch.Tensor, ns: torch.Tensor) -> Non
                      ("h_score", torch.float32), ("h_len", torch.int64), ("h_tokens", torch.int64),
                      ("last_t", torch.int64)):
         _need(f"{what}.{name}", getattr(s, name), dt)
+    mix = [None] * 5
+    if mixed:
+        for name, dt, shape in (("sampling", torch.bool, (B,)), ("samp_tok", torch.int64, (n,)),
+                                ("samp_score", torch.float32, (n,)), ("row_done", torch.bool, (n,)),
+                                ("length", torch.int64, (n,))):
+            _need(f"{what}.{name}", getattr(s, name), dt, shape)
+        mix = [s.sampling.data_ptr(), s.samp_tok.data_ptr(), s.samp_score.data_ptr(), s.row_done.data_ptr(),
+               s.length.data_ptr()]
     dev = s.src.device
     with torch.cuda.device(dev):
-        st = _lib.load().wt_beam_update(
+        st = _lib.load().wt_beam_update_mixed(
             top_s.data_ptr(), top_i.data_ptr(), s.t.data_ptr(), s.pos.data_ptr(), s.sot_pos.data_ptr(),
             ns.data_ptr(), s.no_speech.data_ptr(), s.done.data_ptr(), s.hist.data_ptr(), s.cum.data_ptr(),
             s.src.data_ptr(), s.tokens.data_ptr(), s.forced.data_ptr(), s.h_count.data_ptr(), s.h_score.data_ptr(),
-            s.h_len.data_ptr(), s.h_tokens.data_ptr(), s.last_t.data_ptr(), B, K, c, T, S, s.P, s.cfg.vocab_size,
-            s.cfg.eot, torch.cuda.current_stream(dev).cuda_stream)
+            s.h_len.data_ptr(), s.h_tokens.data_ptr(), s.last_t.data_ptr(), *mix, B, K, c, T, S, s.P,
+            s.cfg.vocab_size, s.cfg.eot, torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st, what)
+
+
+def sample(s) -> None:
+    """Each sampled row's token and its log-probability (``s.samp_tok``, ``s.samp_score``) from the scores
+    :func:`scores` wrote (``s.scores``: the sampled rows' log-probabilities), by Gumbel-max on ``log_probs /
+    temperature`` with the reference's counter-based random numbers (search.uniform) -- the reference's
+    beam_kernels.sample (beam_kernels.py:284-289, kernel :136-167)."""
+    what = "beam_sample"
+    B, K = s.pos.shape[0], s.K
+    n = B * K
+    _need(what, s.scores, torch.float32)
+    if s.scores.shape[0] != n:
+        raise ValueError(f"{what}: scores has {s.scores.shape[0]} rows, expected {n}")
+    v = s.scores.shape[1]
+    for name, dt, shape in (("t", torch.int64, (B,)), ("done", torch.bool, (B,)), ("row_done", torch.bool, (n,)),
+                            ("sampling", torch.bool, (B,)), ("temperature", torch.float32, (B,)),
+                            ("seed", torch.int64, (B,)), ("samp_tok", torch.int64, (n,)),
+                            ("samp_score", torch.float32, (n,))):
+        _need(f"{what}.{name}", getattr(s, name), dt, shape)
+    dev = s.scores.device
+    with torch.cuda.device(dev):
+        st = _lib.load().wt_beam_sample(s.scores.data_ptr(), s.t.data_ptr(), s.done.data_ptr(), s.row_done.data_ptr(),
+                                        s.sampling.data_ptr(), s.temperature.data_ptr(), s.seed.data_ptr(),
+                                        s.samp_tok.data_ptr(), s.samp_score.data_ptr(), B, K, v,
+                                        torch.cuda.current_stream(dev).cuda_stream)
     _lib.check(st, what)
 
 
@@ -162,13 +200,17 @@ def best(s, logits: torch.Tensor, ns: torch.Tensor, out: torch.Tensor | None = N
     _need(what, top_i, torch.int64, (B, 2 * K))
     c = s.cfg
     ts = bool(getattr(s, "timestamps", False))
+    sampling = None
+    if getattr(s, "mixed", False):  # (sampled windows' rows score their log-probabilities alone)
+        _need(f"{what}.sampling", s.sampling, torch.bool, (B,))
+        sampling = s.sampling.data_ptr()
     dev = logits.device
     lib = _lib.load()
     nbytes = int(lib.wt_beam_scores_workspace(B, K))
     ws = _workspace(dev, ("scores", B, K), nbytes)
     with torch.cuda.device(dev):
-        st = lib.wt_beam_scores(logits.data_ptr(), s.suppress.data_ptr(), s.begin.data_ptr(), s.t.data_ptr(),
-                                s.cum.data_ptr(), s.hist.data_ptr(), s.max_initial.data_ptr(), _ptr(out),
+        st = lib.wt_beam_scores_mixed(logits.data_ptr(), s.suppress.data_ptr(), s.begin.data_ptr(), s.t.data_ptr(),
+                                s.cum.data_ptr(), sampling, s.hist.data_ptr(), s.max_initial.data_ptr(), _ptr(out),
                                 ns.data_ptr(), top_s.data_ptr(), top_i.data_ptr(), B, K, v, s.hist.shape[1], int(ts),
                                 c.no_speech, (c.no_timestamps or 0) if ts else 0, (c.timestamp_begin or 0) if ts else 0,
                                 c.eot, ws.data_ptr(), nbytes, torch.cuda.current_stream(dev).cuda_stream)
@@ -191,8 +233,8 @@ def step_bookkeeping(s, logits: torch.Tensor, ns: torch.Tensor) -> None:
 
 
 def install(module) -> None:
-    """Route a reference ``whisper_trt.beam_kernels`` module's beam-mode bookkeeping (``scores``, ``update``) to
-    these kernels (in place), so that the reference's ``Search._body`` (search.py:251-256, ``fused=True``) runs on them
-    unchanged. Sampled slots (``sampling_slots=True``) are refused by :func:`update`."""
-    for name in ("scores", "update"):
+    """Route a reference ``whisper_trt.beam_kernels`` module's bookkeeping (``scores``, ``sample``, ``update``) to
+    these kernels (in place), so that the reference's ``Search._body`` (search.py:251-256, ``fused=True``, with or
+    without sampled slots) runs on them unchanged."""
+    for name in ("scores", "sample", "update"):
         setattr(module, name, globals()[name])
