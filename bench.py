@@ -401,8 +401,12 @@ def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) 
     ms_per_step = t_max / args.steps
     value = total_bytes / (t_max * 1e-3) / 1e9
 
-    # per-kernel device times (roofline): eager launches bracketed by events, queued behind a sleep so the
-    # host stays ahead of the GPU
+    # per-kernel device times (roofline), at the schedule's state in the middle of the timed steps (the schedule
+    # replayed from its start: the offsets the timed steps saw on average)
+    reset_state()
+    for _ in range(args.warmup + args.steps // 2):
+        graph.replay()
+    torch.cuda.synchronize(dev)
     ker = kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch)
 
     # end to end through the public API: H2D of the step's inputs from pinned memory, the step, D2H of its outputs
@@ -428,10 +432,20 @@ def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) 
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": cross_bytes, "launch_us": round(ker["cross_ms"] * 1e3, 2),
+                     "timing": "launch_us: the kernel's 32 layers' launches back to back in a CUDA graph (programmatic "
+                               "dependent launch, as in the step), events around the replays / launches; "
+                               "launch_us_isolated: one launch at a time between events",
+                     "launch_us_isolated": round(ker["cross_iso_ms"] * 1e3, 2),
+                     "frac_isolated": round(cross_bytes / (ker["cross_iso_ms"] * 1e-3) / 1e9 / peak, 4),
                      "traffic": traffic,
                      "self_attn": {"launch_us": round(ker["self_ms"] * 1e3, 2),
                                    "achieved": round(ker["self_bytes"] / (ker["self_ms"] * 1e-3) / 1e9, 1),
-                                   "frac": round(ker["self_bytes"] / (ker["self_ms"] * 1e-3) / 1e9 / peak, 4)}},
+                                   "frac": round(ker["self_bytes"] / (ker["self_ms"] * 1e-3) / 1e9 / peak, 4),
+                                   "launch_us_isolated": round(ker["self_iso_ms"] * 1e3, 2),
+                                   "frac_isolated": round(ker["self_bytes"] / (ker["self_iso_ms"] * 1e-3) / 1e9
+                                                          / peak, 4),
+                                   "algorithmic_bytes_per_launch": ker["self_bytes"],
+                                   "mean_cached_positions": round(ker["mean_cached_positions"], 1)}},
         "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
     }
     if e2e is not None:
@@ -471,6 +485,49 @@ def gpu_index(local_rank: int) -> int:
 
 
 def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch, reps: int = 3) -> dict:
+    """Device time per launch of each attention kernel, two ways (CUDA events on the launching stream, warm):
+
+    * chained -- each kernel alone, its 32 layers' launches back to back in a CUDA graph (with programmatic dependent
+      launch, as in the step: a launch's start overlaps its predecessor's drain), events around the replays / 32;
+    * isolated -- one launch at a time between events, self and cross alternating (no overlap: every launch pays
+      its own ramp-up and drain).
+
+    Algorithmic bytes use the offsets as they stand (after the timed steps)."""
+
+    def graph_of(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    def chained(fn) -> float:
+        g = graph_of(fn)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        del g
+        return e0.elapsed_time(e1) / (reps * L)
+
+    def self_all():
+        for i in range(L):
+            ap.self_attn_step_triton(qkv[i], cache[i, 0], cache[i, 1], offset, src, out=y_self[i])
+
+    def cross_all():
+        for i in range(L):
+            ap.cross_attn_triton(q[i], cross[i, 0], cross[i, 1], out=y_cross[i])
+
+    self_chain, cross_chain = chained(self_all), chained(cross_all)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps * L)]
     torch.cuda.synchronize(dev)
     torch.cuda._sleep(200_000_000)
@@ -483,10 +540,12 @@ def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, 
             ap.cross_attn_triton(q[i], cross[i, 0], cross[i, 1], out=y_cross[i])
             e[2].record()
     torch.cuda.synchronize(dev)
-    self_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in evs]))
-    cross_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs]))
     offs = offset.cpu().numpy()[:: sch.K]  # (a window's rows share its offset)
-    return {"self_ms": self_ms, "cross_ms": cross_ms, "self_bytes": sch.self_launch_bytes(offs, append=False)}
+    return {"self_ms": self_chain, "cross_ms": cross_chain,
+            "self_iso_ms": float(np.mean([e[0].elapsed_time(e[1]) for e in evs])),
+            "cross_iso_ms": float(np.mean([e[1].elapsed_time(e[2]) for e in evs])),
+            "self_bytes": sch.self_launch_bytes(offs, append=False),
+            "mean_cached_positions": float(offs.mean())}
 
 
 def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_state, sch, warmup,
