@@ -831,10 +831,11 @@ def run_reference(args, world: int) -> dict:
 
 
 def run_reference_gpu(local_rank: int, reps: int = 10) -> dict:
-    """The reference's own GPU kernels beside this package's, on this GPU and the same inputs: the decode step's
-    attention of 32 layers as its TritonDecoderBackend sequences it (self_attn_step_triton with the append, then
-    cross_attn_split_triton + cross_attn_combine_triton per layer) at config 3 and config 2, each side captured in
-    a CUDA graph (``benchmarks/triton_baseline.py``'s ``step`` section), with the clocks of the run."""
+    """The reference's own GPU kernels beside this package's, on this GPU and the same inputs, at config 3 and
+    config 2, each side captured in a CUDA graph (``benchmarks/triton_baseline.py``'s ``step`` and ``decoder_step``
+    sections), with the clocks of the run: the decode step's attention of 32 layers as its TritonDecoderBackend
+    sequences it (self_attn_step_triton with the append, then cross_attn_split_triton + cross_attn_combine_triton per
+    layer), and the whole decode step through that backend itself."""
     R = reference_module()
     if R is None or getattr(R, "triton", None) is None:
         return {"unavailable": "the reference package (baseline/_ref) or Triton is not available"}
@@ -849,15 +850,24 @@ def run_reference_gpu(local_rank: int, reps: int = 10) -> dict:
     sampler = ClockSampler(gpu_index(local_rank))
     t0 = time.time()
     out = {}
+    from whisper_trt_b200 import decoder_kernels
+
+    ours = SimpleNamespace(attn_plugin=attn_plugin, decoder_kernels=decoder_kernels)
     for name in ("config3", "config2"):
-        r = tb.step(R, SimpleNamespace(attn_plugin=attn_plugin), name, reps)
+        r = tb.step(R, ours, name, reps)
         out[name] = {k: r[k] for k in ("rows", "cached_mean", "bytes_per_step", "ref_step_us", "ref_step_unsplit_us",
                                        "ours_step_us", "ref_step_gbs", "ours_step_gbs", "speedup_vs_ref_step",
                                        "speedup_vs_ref_step_unsplit", "max_abs_diff")}
         torch.cuda.empty_cache()
+        out[name]["decoder_step"] = {k: v for k, v in tb.decoder_step(R, ours, name, reps).items()
+                                     if k not in ("section", "workload")}
+        torch.cuda.empty_cache()
     out["clocks"] = sampler.stop(t0, time.time())
     out["how"] = ("device time per step of CUDA-graph replays (10 after 3 warm-up), the same seeded inputs and static "
-                  "offsets on both sides, no bookkeeping; the reference's Triton 3.6 kernels from baseline/_ref")
+                  "offsets on both sides; attention alone (no bookkeeping), and decoder_step: the whole 32-layer decode "
+                  "step through the reference's own TritonDecoderBackend (random-init whisper-large-v3 decoder), as it "
+                  "ships (ref_cublas) and with this package installed (ours_attn: attention + logits32; ours_whole: "
+                  "also the fused linear layers); the reference's Triton 3.6 kernels from baseline/_ref")
     return out
 
 

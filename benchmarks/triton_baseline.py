@@ -20,7 +20,9 @@ Sections (whisper-large-v3 shapes: 20 heads x 64, d 1280, 1500 frames, 32 layers
 * ``logits32``: ``logits32_triton`` at 160 rows (attn_plugin.py:549-560);
 * ``prompt``: ``self_attn_triton`` at 80 rows x a 224-token prompt (attn_plugin.py:462-479);
 * ``beam``: ``beam_kernels.scores`` + the step's ``topk`` (search.py:252-253) against ``slots.best`` at 32 x 5 rows;
-* ``decoder``: ``decoder_kernels.ln_linear`` / ``linear_residual`` (autotuned on first call) at 160 rows.
+* ``decoder``: ``decoder_kernels.ln_linear`` / ``linear_residual`` (autotuned on first call) at 160 rows;
+* ``decoder_step``: the whole decode step through the reference's own ``TritonDecoderBackend`` (its kernels, and
+  this package installed into its modules) at config 2 and config 3.
 """
 
 from __future__ import annotations
@@ -288,12 +290,95 @@ def decoder(RD, ours, reps: int, rows: int = 160, d: int = 1280) -> dict:
     return res
 
 
+LARGE_V3 = dict(n_mels=128, d_model=1280, enc_layers=32, enc_heads=20, enc_ffn=5120, dec_layers=32, dec_heads=20,
+                dec_ffn=5120, vocab_size=51866)
+
+
+def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -> dict:
+    """The whole decode step: the reference's own ``TritonDecoderBackend.step_fn`` closure (runtime.py:125-174) on
+    a whisper-large-v3-shaped random-init decoder (``modeling.Decoder(cfg)``, fp16), captured in a CUDA graph and
+    replayed: 32 layers of LayerNorm, QKV, self-attention with the append, out-projection, LayerNorm, query,
+    cross-attention, out-projection, MLP; the final LayerNorm and the vocabulary projection. Variants:
+
+    * ``ref_cublas``: the reference as it ships (its Triton attention and LayerNorm kernels, cuBLAS GEMMs, its
+      logits32 kernel);
+    * ``ours_attn``: the same backend with this package installed into its ``attn_plugin`` (attention, logits32);
+    * ``ours_whole``: its ``gemm="triton"`` variant with this package installed into ``attn_plugin`` and
+      ``decoder_kernels``: every kernel of the step but the embedding gather, the final LayerNorm and one cast;
+    * ``ref_triton`` (with ``ref_gemm_triton``): the reference's own ``gemm="triton"`` variant (autotunes first).
+
+    The ``gemm="triton"`` variants leave the new keys/values in ``new_kv`` for the search to scatter (the cuBLAS
+    variant appends them itself). Inputs: the workload's rows and cache lengths, window-local random slot tables."""
+    from whisper_trt import config as RC
+    from whisper_trt import decoder_kernels as RDK
+    from whisper_trt import modeling as RM
+    from whisper_trt import runtime as RR
+
+    c = STEP_CONFIGS[name]
+    W, K, C = c["windows"], c["beams"], c["capacity"]
+    N = W * K
+    cfg = RC.WhisperConfig(**LARGE_V3)
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        dec = RM.Decoder(cfg)
+    dec = dec.half().eval().requires_grad_(False)
+    model = SimpleNamespace(cfg=cfg, decoder=dec)
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    tokens = torch.randint(0, 50000, (N, 1), generator=g, device=dev)
+    off = torch.randint(c["lo"], c["hi"] + 1, (W,), generator=g, device=dev).repeat_interleave(K)
+    src = ((torch.arange(N, device=dev) // K * K)[:, None]
+           + torch.randint(0, K, (N, C), generator=g, device=dev)).to(torch.int32)
+    cache = torch.randn(L, 2, N, H, C, D, generator=g, device=dev, dtype=torch.float16)
+    cross = torch.randn(L, 2, W, H, T, D, generator=g, device=dev, dtype=torch.float16)
+    logits = torch.empty(N, 1, cfg.vocab_size, device=dev)
+    new_kv = torch.empty(L, 2, N, H, 1, D, device=dev, dtype=torch.float16)
+    saved = [(m, dict(vars(m))) for m in (R, RDK)]
+
+    def restore():
+        for m, names in saved:
+            for k, v in names.items():
+                setattr(m, k, v)
+
+    variants = [("ref_cublas", "cublas", False, False), ("ours_attn", "cublas", True, False),
+                ("ours_whole", "triton", True, True)]
+    if ref_gemm_triton:
+        variants.append(("ref_triton", "triton", False, False))
+    out = {"section": "decoder_step", "workload": name, "rows": N, "windows": W, "capacity": C,
+           "cached_mean": round(float(off.float().mean()), 1)}
+    logit_ref = None
+    for label, gemm, attn, lin in variants:
+        try:
+            if attn:
+                ours.attn_plugin.install(R)
+            if lin:
+                ours.decoder_kernels.install(RDK)
+            backend = RR.TritonDecoderBackend(model, encoder=None, gemm=gemm)
+            cache_v = cache.clone()
+            run = backend.step_fn(tokens, off, cache_v, logits, new_kv, src, cross)
+            t = _time(run, reps)
+        finally:
+            restore()
+        lg = logits.clone()
+        if logit_ref is None:
+            logit_ref = lg
+        out[f"{label}_us"] = round(t * 1e6, 1)
+        out[f"{label}_max_logit_diff_vs_ref_cublas"] = _maxdiff(lg, logit_ref)
+        del cache_v, backend, run
+        torch.cuda.empty_cache()
+    out["speedup_ours_attn"] = round(out["ref_cublas_us"] / out["ours_attn_us"], 3)
+    out["speedup_ours_whole"] = round(out["ref_cublas_us"] / out["ours_whole_us"], 3)
+    return out
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--ref", default="baseline/_ref", help="directory holding the reference's whisper_trt package")
-    p.add_argument("--sections", default="step,logits32,prompt,beam,decoder")
+    p.add_argument("--sections", default="step,logits32,prompt,beam,decoder,decoder_step")
     p.add_argument("--workloads", default="config3,config2")
     p.add_argument("--reps", type=int, default=10)
+    p.add_argument("--ref-gemm-triton", action="store_true",
+                   help="decoder_step: also time the reference's own gemm='triton' variant (autotunes first)")
     a = p.parse_args()
     ref = Path(a.ref).resolve()
     if not (ref / "whisper_trt" / "attn_plugin.py").is_file():
@@ -324,6 +409,10 @@ def main() -> None:
             print(json.dumps(beam(RB, ours, a.reps)), flush=True)
         elif sec == "decoder":
             print(json.dumps(decoder(RD, ours, a.reps)), flush=True)
+        elif sec == "decoder_step":
+            for wl in a.workloads.split(","):
+                print(json.dumps(decoder_step(R, ours, wl, a.reps, ref_gemm_triton=a.ref_gemm_triton)), flush=True)
+                torch.cuda.empty_cache()
         else:
             raise SystemExit(f"unknown section {sec!r}")
         torch.cuda.empty_cache()
