@@ -123,6 +123,16 @@ int wt_self_attn(int dtype, const void *qkv, const void *k_cache, const void *v_
  * ------------------------------------------------------------------------------------------------------- */
 int wt_cross_attn_split(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
                         int queries, int heads, int frames, int head_dim, int splits, void *stream);
+/* wt_cross_attn_split_ws: wt_cross_attn_split (the same part, the same reference function) on the persistent
+ *   stream-K TMA kernel of wt_cross_attn, its units the (window, head, slice) triples: it streams the keys at the
+ *   fused kernel's rate where the per-slice kernel of wt_cross_attn_split takes one CTA per slice. Needs a workspace
+ *   of wt_cross_attn_split_workspace() bytes (the per-shape rule of wt_cross_attn's); that size is 0 for shapes the
+ *   stream-K kernel does not take (a 16-key block of some slice would hold no key, e.g. T < 16 * splits), which run
+ *   the per-slice kernel and need no workspace. */
+size_t wt_cross_attn_split_workspace(int windows, int queries, int heads, int frames, int head_dim, int splits);
+int wt_cross_attn_split_ws(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
+                           int queries, int heads, int frames, int head_dim, int splits, void *workspace,
+                           size_t workspace_bytes, void *stream);
 int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, int queries, int heads,
                           int head_dim, int splits, void *stream);
 size_t wt_cross_attn_workspace(int windows, int queries, int heads, int frames, int head_dim);

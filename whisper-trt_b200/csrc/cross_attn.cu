@@ -24,9 +24,10 @@
 namespace wt {
 
 // the fused kernel (cross_stream.cu)
-size_t cross_stream_workspace(int W, int S, int H, int Tn);
+size_t cross_stream_workspace(int W, int S, int H, int Tn, int P);
+bool cross_stream_slices_ok(int Tn, int P);
 int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y, int W, int S, int H, int Tn,
-                 void *workspace, size_t workspace_bytes, void *stream);
+                 void *workspace, size_t workspace_bytes, void *stream, int P = 0, float *slices_out = nullptr);
 
 namespace {
 
@@ -302,6 +303,30 @@ int wt_cross_attn_split(int dtype, const void *q, const void *k, const void *v, 
                                             splits, stream);
 }
 
+size_t wt_cross_attn_split_workspace(int windows, int queries, int heads, int frames, int head_dim, int splits) {
+  if (windows <= 0 || queries <= 0 || heads <= 0 || frames <= 0 || head_dim != wt::kD || splits <= 0) return 0;
+  if (!wt::cross_stream_slices_ok(frames, splits)) return 0;  // (the per-slice kernel, which needs none)
+  return wt::cross_stream_workspace(windows, queries, heads, frames, splits);
+}
+
+int wt_cross_attn_split_ws(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
+                           int queries, int heads, int frames, int head_dim, int splits, void *workspace,
+                           size_t workspace_bytes, void *stream) {
+  using namespace wt;
+  int st = check_cross("cross_attn_split", dtype, q, k, v, part, windows, queries, heads, frames, head_dim);
+  if (st != WT_OK) return st;
+  WT_REQUIRE(splits > 0 && splits <= 65535, WT_ERR_ARG, "cross_attn_split: splits %d", splits);
+  const size_t need = wt_cross_attn_split_workspace(windows, queries, heads, frames, head_dim, splits);
+  if (need == 0)
+    return wt_cross_attn_split(dtype, q, k, v, part, windows, queries, heads, frames, head_dim, splits, stream);
+  WT_REQUIRE(workspace && workspace_bytes >= need, WT_ERR_WORKSPACE,
+             "cross_attn_split: needs a zeroed workspace of %zu bytes (given %zu)", need,
+             workspace ? workspace_bytes : 0);
+  WT_ALIGNED(workspace);
+  return cross_stream(dtype, q, k, v, part, windows, queries, heads, frames, workspace, workspace_bytes, stream,
+                      splits, part);
+}
+
 int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, int queries, int heads,
                           int head_dim, int splits, void *stream) {
   using namespace wt;
@@ -323,7 +348,7 @@ int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, in
 
 size_t wt_cross_attn_workspace(int windows, int queries, int heads, int frames, int head_dim) {
   if (windows <= 0 || queries <= 0 || heads <= 0 || frames <= 0 || head_dim != wt::kD) return 0;
-  return wt::cross_stream_workspace(windows, queries, heads, frames);
+  return wt::cross_stream_workspace(windows, queries, heads, frames, 0);
 }
 
 int wt_cross_attn(int dtype, const void *q, const void *k, const void *v, void *y, int windows, int queries,

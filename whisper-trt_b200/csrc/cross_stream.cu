@@ -60,6 +60,8 @@ struct StreamArgs {
   float *part;
   int *counters;
   int *err;
+  float *slices_out;  // slice mode: the reference's partials [W, H, P, S, D + 2] instead of y (null: fused output)
+  int P, chunk;       // key slices per (window, head) and keys per slice (fused: 1 and Tn)
   int W, S, H, Tn, QG, bpu;
   long long total;
   long long per_warp;
@@ -74,6 +76,27 @@ __host__ __device__ inline long long first_warp(long long u, int bpu, long long 
 }
 __host__ __device__ inline long long last_warp(long long u, int bpu, long long per_warp) {
   return ((u + 1) * bpu - 1) / per_warp;
+}
+
+// A unit u = ((window * H + head) * P + slice) * QG + query group.
+struct UnitPos {
+  int w, h, sl, qg;
+};
+__device__ __forceinline__ UnitPos unit_pos(const StreamArgs &a, long long u) {
+  UnitPos p;
+  p.qg = static_cast<int>(u % a.QG);
+  const long long r = u / a.QG;
+  p.sl = static_cast<int>(r % a.P);
+  const int wh = static_cast<int>(r / a.P);
+  p.w = wh / a.H;
+  p.h = wh - p.w * a.H;
+  return p;
+}
+
+// Slice mode: one query's slice partial (unnormalised acc[64], running maximum m in log2 units, sum of exponentials l)
+// into the reference's part layout [W, H, P, S, D + 2].
+__device__ __forceinline__ float *slice_record(const StreamArgs &a, const UnitPos &p, int qi) {
+  return a.slices_out + ((((static_cast<size_t>(p.w) * a.H + p.h) * a.P + p.sl) * a.S + qi) * (kD + 2));
 }
 
 template <int NT>
@@ -138,8 +161,8 @@ __device__ __forceinline__ bool publish(const StreamArgs &a, long long u, int nb
 template <typename T, int NT>
 __device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a, long long u, int lane) {
   const int g = lane >> 2, c = lane & 3;
-  const int wh = static_cast<int>(u / a.QG), qg = static_cast<int>(u % a.QG);
-  const int w = wh / a.H, h = wh - w * a.H;
+  const UnitPos p = unit_pos(a, u);
+  const int w = p.w, h = p.h, qg = p.qg;
   const size_t HD = static_cast<size_t>(a.H) * kD;
   T *y = static_cast<T *>(a.y);
 #pragma unroll
@@ -150,7 +173,18 @@ __device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
       const int qi = qg * NT * 8 + nt * 8 + 2 * c + j;
-      if (qi < a.S) {
+      if (qi < a.S && a.slices_out != nullptr) {  // slice mode: the slice's unnormalised partial
+        float *rec = slice_record(a, p, qi);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          rec[16 * i + g] = st.o[nt][i][j];
+          rec[16 * i + g + 8] = st.o[nt][i][j + 2];
+        }
+        if (g == 0) {
+          rec[kD] = st.m[nt][j];
+          rec[kD + 1] = l;
+        }
+      } else if (qi < a.S) {
         const float inv = 1.f / l;
         T *yr = y + (static_cast<size_t>(w) * a.S + qi) * HD + static_cast<size_t>(h) * kD;
 #pragma unroll
@@ -172,8 +206,8 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
   __syncwarp();  // (after lane 0's acquire-release count: every lane's loads below are ordered after it)
   const long long fw = first_warp(u, a.bpu, a.per_warp);
   const int nslots = static_cast<int>(last_warp(u, a.bpu, a.per_warp) - fw + 1);
-  const int wh = static_cast<int>(u / a.QG), qg = static_cast<int>(u % a.QG);
-  const int w = wh / a.H, h = wh - w * a.H;
+  const UnitPos up = unit_pos(a, u);
+  const int w = up.w, h = up.h, qg = up.qg;
   const int q0 = qg * NT * 8;
   const int nq = min(NT * 8, a.S - q0);
   const float *base = a.part + static_cast<size_t>(u) * a.max_slots * (NT * 8) * kPart;
@@ -242,7 +276,16 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int idx = lane + 32 * (it0 + k), qq = idx >> 3, d8 = idx & 7;
-      if (qq < nq) {
+      if (qq < nq && a.slices_out != nullptr) {  // slice mode: the combined, still unnormalised partial
+        float *rec = slice_record(a, up, q0 + qq);  // (records of D + 2 floats: 8-byte aligned)
+#pragma unroll
+        for (int i = 0; i < 8; i += 2)
+          *reinterpret_cast<float2 *>(rec + 8 * d8 + i) = make_float2(num[k][i], num[k][i + 1]);
+        if (d8 == 0) {
+          rec[kD] = top[k];
+          rec[kD + 1] = den[k];
+        }
+      } else if (qq < nq) {
         const float inv = 1.f / den[k];
 #pragma unroll
         for (int i = 0; i < 8; ++i) num[k][i] *= inv;
@@ -322,7 +365,8 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
 
   // the range's position as (window-head, query group, block), advanced without divisions
   const long long u0 = n ? beg / a.bpu : 0;
-  int i_wh = static_cast<int>(u0 / a.QG), i_qg = static_cast<int>(u0 % a.QG);
+  int i_qg = static_cast<int>(u0 % a.QG), i_sl = static_cast<int>((u0 / a.QG) % a.P);
+  int i_wh = static_cast<int>(u0 / a.QG / a.P);
   int i_b = static_cast<int>(beg - u0 * a.bpu);
   int issued = 0;
   // (the bounded-wait test hook: warp 0 of CTA 0 issues nothing for its first stage, whose wait then runs out)
@@ -330,7 +374,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   auto issue_next = [&]() {  // lane 0: the next block of the range into its stage
     const int s = issued % kStreamStages;
     unsigned char *dst = ring + s * kStageBytes;
-    const int row = i_wh * a.Tn + i_b * 16;
+    const int row = i_wh * a.Tn + i_sl * a.chunk + i_b * 16;
     if (!(withhold && issued == 0)) {
       mbar_arrive_expect_tx(&bars[s], kStageBytes);
       tma_load_2d(dst, &kmap, 0, row, &bars[s]);
@@ -341,7 +385,10 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
       i_b = 0;
       if (++i_qg == a.QG) {
         i_qg = 0;
-        ++i_wh;
+        if (++i_sl == a.P) {
+          i_sl = 0;
+          ++i_wh;
+        }
       }
     }
   };
@@ -372,7 +419,8 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
     req_u[warp] = -1;
     mbar_arrive(&req_bar[warp]);
   }
-  int c_wh = static_cast<int>(u0 / a.QG), c_qg = static_cast<int>(u0 % a.QG);
+  int c_qg = static_cast<int>(u0 % a.QG), c_sl = static_cast<int>((u0 / a.QG) % a.P);
+  int c_wh = static_cast<int>(u0 / a.QG / a.P);
   int c_b = static_cast<int>(beg - u0 * a.bpu);
   long long c_u = u0;
   for (int j = 0; j < n;) {
@@ -405,7 +453,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
       int n_wh = c_wh, n_qg = c_qg + 1;
       if (n_qg == a.QG) {
         n_qg = 0;
-        ++n_wh;
+        if (c_sl + 1 == a.P) ++n_wh;
       }
       if (n_wh < a.W * a.H) {
         const int w = n_wh / a.H, h = n_wh - w * a.H;
@@ -421,6 +469,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
     uint32_t ka[4][4], va[4][4];
     smem_frags(ka, va, ring + s0 * kStageBytes, ring + s0 * kStageBytes + kTileBytes, lane);
     const int k0 = c_b * 16;
+    const int klen = min(a.Tn - c_sl * a.chunk, a.chunk);  // keys of the unit's slice (fused: all Tn)
     const int used = pair ? 2 : 1;
     if (pair) {
       const int s1 = (j + 1) % kStreamStages;
@@ -436,13 +485,13 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
       __syncwarp();
       if (lane == 0)
         for (int u = 0; u < used && issued < n; ++u) issue_next();
-      const bool ok[2][2] = {{k0 + g < a.Tn, k0 + g + 8 < a.Tn}, {k0 + 16 + g < a.Tn, k0 + 24 + g < a.Tn}};
+      const bool ok[2][2] = {{k0 + g < klen, k0 + g + 8 < klen}, {k0 + 16 + g < klen, k0 + 24 + g < klen}};
       attend_block2<T, NT>(st, ka, va, kb, vb, qf, ok, a.scale);
     } else {
       consume_frags(ka, va);
       __syncwarp();
       if (lane == 0 && issued < n) issue_next();
-      attend_block<T, NT>(st, ka, va, qf, k0 + g < a.Tn, k0 + g + 8 < a.Tn, a.scale);
+      attend_block<T, NT>(st, ka, va, qf, k0 + g < klen, k0 + g + 8 < klen, a.scale);
     }
     nblk += used;
     j += used;
@@ -452,7 +501,10 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
       ++c_u;
       if (++c_qg == a.QG) {
         c_qg = 0;
-        ++c_wh;
+        if (++c_sl == a.P) {
+          c_sl = 0;
+          ++c_wh;
+        }
       }
     }
   }
@@ -493,17 +545,21 @@ int forced_shape() {
 }
 
 struct StreamPlan {
-  int nt, qgs, bpu, max_slots, grid, shape;
+  int nt, qgs, bpu, max_slots, grid, shape, slices, chunk;
   long long units, total, per_warp;
   size_t counters_off, part_off, bytes;
 };
 
-StreamPlan plan_stream(int W, int S, int H, int Tn) {
+// P = 0: the fused attention (a unit is a whole (window, head, query group)); P > 0: slice mode, P key slices of
+// ceil(Tn / P) keys per (window, head), each its own unit.
+StreamPlan plan_stream(int W, int S, int H, int Tn, int P) {
   StreamPlan p{};
   p.nt = (S + 7) / 8 > 4 ? 4 : (S + 7) / 8;
   p.qgs = (S + p.nt * 8 - 1) / (p.nt * 8);
-  p.bpu = (Tn + 15) / 16;
-  p.units = static_cast<long long>(W) * H * p.qgs;
+  p.slices = P > 0 ? P : 1;
+  p.chunk = P > 0 ? (Tn + P - 1) / P : Tn;
+  p.bpu = (p.chunk + 15) / 16;
+  p.units = static_cast<long long>(W) * H * p.slices * p.qgs;
   p.total = p.units * p.bpu;
   if (p.nt >= 2) {
     p.shape = 0;  // (more query tiles: one block per step keeps them in registers)
@@ -558,11 +614,18 @@ int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamA
 
 }  // namespace
 
-size_t cross_stream_workspace(int W, int S, int H, int Tn) { return plan_stream(W, S, H, Tn).bytes; }
+size_t cross_stream_workspace(int W, int S, int H, int Tn, int P) { return plan_stream(W, S, H, Tn, P).bytes; }
+
+bool cross_stream_slices_ok(int Tn, int P) {
+  // every 16-key block of every slice holds at least one key (the block math needs one)
+  if (P <= 0) return false;
+  const int chunk = (Tn + P - 1) / P, bpu = (chunk + 15) / 16;
+  return Tn - (P - 1) * chunk > 16 * (bpu - 1);
+}
 
 int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y, int W, int S, int H, int Tn,
-                 void *workspace, size_t workspace_bytes, void *stream) {
-  const StreamPlan p = plan_stream(W, S, H, Tn);
+                 void *workspace, size_t workspace_bytes, void *stream, int P, float *slices_out) {
+  const StreamPlan p = plan_stream(W, S, H, Tn, P);
   WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,
              "cross_attn: needs a zeroed workspace of %zu bytes (given %zu)", p.bytes, workspace ? workspace_bytes : 0);
   WT_REQUIRE(p.total < (1LL << 40), WT_ERR_ARG, "cross_attn: too large");
@@ -574,7 +637,8 @@ int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y
   if (st != WT_OK) return st;
   char *ws = static_cast<char *>(workspace);
   StreamArgs a{q,       y,    reinterpret_cast<float *>(ws + p.part_off), reinterpret_cast<int *>(ws + p.counters_off),
-               reinterpret_cast<int *>(ws), W, S, H, Tn, p.qgs, p.bpu, p.total, p.per_warp, p.max_slots,
+               reinterpret_cast<int *>(ws), P > 0 ? slices_out : nullptr, p.slices, p.chunk, W, S, H, Tn, p.qgs,
+               p.bpu, p.total, p.per_warp, p.max_slots,
                static_cast<float>(1.0 / 8.0 * 1.4426950408889634), wait_limit(), test_withhold_stage()};
   const bool bf = dtype == WT_BF16;
   const int g = p.grid, sh = p.shape;

@@ -31,6 +31,9 @@ SIGNATURES = {
                              c_void]),
     "wt_cross_attn_split": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_int,
                                     c_void]),
+    "wt_cross_attn_split_workspace": (c_size, [c_int] * 6),
+    "wt_cross_attn_split_ws": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int,
+                                       c_int, c_void, c_size, c_void]),
     "wt_cross_attn_combine": (c_int, [c_int, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void]),
     "wt_cross_attn_workspace": (c_size, [c_int, c_int, c_int, c_int, c_int]),
     "wt_cross_attn": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_void,

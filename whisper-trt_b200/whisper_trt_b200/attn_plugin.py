@@ -152,7 +152,8 @@ def self_attn_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     read through ``src``, and causally over the new tokens -> [N, S, H*D] in qkv's dtype. The caches are only read
     (the caller stores the new keys/values). Reference: attn_plugin.py:462-479 (kernel :275-307, op :102-121).
 
-    ``config`` is accepted for call-compatibility and ignored (one launch shape: 64 queries per CTA)."""
+    ``config`` is accepted for call-compatibility and ignored (64 queries per CTA; one new token per row goes to
+    the decode-step kernel, which computes the same op)."""
     what = "self_attn"
     if qkv.dim() != 3:
         raise ValueError(f"{what}: qkv must be [N, S, 3*H*D]")
@@ -175,6 +176,8 @@ def self_attn_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
         raise ValueError(f"{what}: out must be [N, S, H*D] of qkv's dtype")
     if s == 0:
         return y
+    if s == 1:  # one new token per row (the reference's gemm="triton" decode step calls this op so): the step kernel
+        return self_attn_step_triton(qkv, k_cache, v_cache, offset, src, out=y)
     with torch.cuda.device(dev):
         st = _lib.load().wt_self_attn(code, qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), offset.data_ptr(),
                                       src.data_ptr(), y.data_ptr(), n, s, h, c, d, _stream(dev))
@@ -236,15 +239,20 @@ def cross_attn_split_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, c
                             splits: int = SPLITS, out: torch.Tensor | None = None) -> torch.Tensor:
     """Partial attention of q [W, S, H*D] over ``splits`` slices (chunk = ceil(T / splits)) of k/v [W, H, T, D]:
     per slice the unnormalised output, the maximum score (log2 units) and the sum of exponentials ->
-    [W, H, splits, S, D + 2] float32. Reference: attn_plugin.py:521-534 (kernel :378-409)."""
+    [W, H, splits, S, D + 2] float32. Reference: attn_plugin.py:521-534 (kernel :378-409). Runs on the stream-K TMA
+    kernel of :func:`cross_attn_triton` with the (window, head, slice) triples as its units (a per-device
+    workspace per shape, as that function's), or, for shapes it does not take, on the per-slice kernel."""
     what = "cross_attn_split"
     w, s, h, t, d, code, dev = _check_cross(what, q, k, v)
     part = q.new_empty(w, h, splits, s, d + 2, dtype=torch.float32) if out is None else out
     if part.shape != (w, h, splits, s, d + 2) or part.dtype != torch.float32:
         raise ValueError(f"{what}: out must be [W, H, splits, S, D+2] float32")
+    lib = _lib.load()
+    nbytes = int(lib.wt_cross_attn_split_workspace(w, s, h, t, d, splits))  # (0: the per-slice kernel, no workspace)
+    ws = _workspace(dev, "cross", (w, s, h, t, d, splits), nbytes).data_ptr() if nbytes else None
     with torch.cuda.device(dev):
-        st = _lib.load().wt_cross_attn_split(code, q.data_ptr(), k.data_ptr(), v.data_ptr(), part.data_ptr(), w, s,
-                                             h, t, d, splits, _stream(dev))
+        st = lib.wt_cross_attn_split_ws(code, q.data_ptr(), k.data_ptr(), v.data_ptr(), part.data_ptr(), w, s, h, t, d,
+                                        splits, ws, nbytes, _stream(dev))
     _lib.check(st, what)
     return part
 
