@@ -200,32 +200,68 @@ __global__ void __launch_bounds__(kCrossThreads)
 }
 
 // part [W, H, P, S, D+2] -> y [W, S, H*D]: one CTA per (window, head)
+// The reference's combine (attn_plugin.py:182-194) of part [W, H, P, S, D + 2]: one thread per (window, head, query,
+// 8-dim chunk of the output), every slice's loads of a pass of up to 8 slices issued before they are folded into a
+// running (top, num, den) -- one L2 round trip per pass; slices without keys (m = -inf) weigh 0.
 template <typename T>
 __global__ void __launch_bounds__(128)
-    combine_kernel(const float *__restrict__ part, T *__restrict__ y, int S, int H, int P) {
-  const int wh = blockIdx.x;
-  const int w = wh / H, h = wh - w * H;
-  const size_t HD = static_cast<size_t>(H) * kD;
+    combine_kernel(const float *__restrict__ part, T *__restrict__ y, int W, int S, int H, int P) {
+  constexpr int kPass = 8;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   pdl_wait();
-  const float *base = part + static_cast<size_t>(wh) * P * S * (kD + 2);
-  for (int idx = threadIdx.x; idx < S * (kD / 8); idx += blockDim.x) {
-    const int s = idx / (kD / 8), d8 = idx - s * (kD / 8);
-    float top = kNegInf;
-    for (int i = 0; i < P; ++i) top = fmaxf(top, base[(i * S + s) * (kD + 2) + kD]);
-    float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
-    for (int i = 0; i < P; ++i) {
-      const float *ps = base + (i * S + s) * (kD + 2);
-      const float ms = ps[kD];
-      const float wgt = (ms == kNegInf) ? 0.f : exp2f(ms - top);  // slices without keys: weight 0
-      den = fmaf(wgt, ps[kD + 1], den);
+  if (idx < static_cast<long long>(W) * H * S * (kD / 8)) {
+    const int d8 = static_cast<int>(idx % (kD / 8));
+    const long long r = idx / (kD / 8);
+    const int s = static_cast<int>(r % S);
+    const int wh = static_cast<int>(r / S);
+    const int w = wh / H, h = wh - w * H;
+    const size_t rec = kD + 2;  // (records of D + 2 floats: 8-byte aligned)
+    const float *base = part + (static_cast<size_t>(wh) * P * S + s) * rec;
+    float top = kNegInf, den = 0.f, num[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i0 = 0; i0 < P; i0 += kPass) {
+      float ms[kPass], ls[kPass];
+      float2 a[kPass][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) num[j] = fmaf(wgt, ps[8 * d8 + j], num[j]);
+      for (int i = 0; i < kPass; ++i) {
+        if (i0 + i < P) {
+          const float *ps = base + static_cast<size_t>(i0 + i) * S * rec;
+          const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ps + kD));
+          ms[i] = ml.x;
+          ls[i] = ml.y;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) a[i][j] = __ldcg(reinterpret_cast<const float2 *>(ps + 8 * d8 + 2 * j));
+        } else {
+          ms[i] = kNegInf;
+          ls[i] = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) a[i][j] = make_float2(0.f, 0.f);
+        }
+      }
+      float pt = top;
+#pragma unroll
+      for (int i = 0; i < kPass; ++i) pt = fmaxf(pt, ms[i]);
+      if (pt == kNegInf) continue;  // (no keys yet)
+      const float f = top == kNegInf ? 0.f : exp2f(top - pt);
+      den *= f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) num[j] *= f;
+      top = pt;
+#pragma unroll
+      for (int i = 0; i < kPass; ++i) {
+        const float wgt = ms[i] == kNegInf ? 0.f : exp2f(ms[i] - top);
+        den = fmaf(wgt, ls[i], den);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          num[2 * j] = fmaf(wgt, a[i][j].x, num[2 * j]);
+          num[2 * j + 1] = fmaf(wgt, a[i][j].y, num[2 * j + 1]);
+        }
+      }
     }
     const float inv = 1.f / den;
 #pragma unroll
     for (int j = 0; j < 8; ++j) num[j] *= inv;
-    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + s) * HD + static_cast<size_t>(h) * kD + 8 * d8) =
-        pack8<T>(num);
+    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + s) * static_cast<size_t>(H) * kD +
+                               static_cast<size_t>(h) * kD + 8 * d8) = pack8<T>(num);
   }
   pdl_launch_dependents();
 }
@@ -336,13 +372,15 @@ int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, in
   WT_ALIGNED(part);
   WT_ALIGNED(y);
   WT_REQUIRE(head_dim == kD, WT_ERR_UNSUPPORTED, "cross_attn_combine: head_dim %d (this build: 64)", head_dim);
-  const dim3 grid(windows * heads), block(128);
+  const long long items = static_cast<long long>(windows) * heads * queries * (kD / 8);
+  WT_REQUIRE((items + 127) / 128 < (1LL << 31), WT_ERR_ARG, "cross_attn_combine: too large");
+  const dim3 grid(static_cast<unsigned>((items + 127) / 128)), block(128);
   if (dtype == WT_F16)
     return launch("cross_attn_combine", combine_kernel<__half>, grid, block, 0, stream, part,
-                  static_cast<__half *>(y), queries, heads, splits);
+                  static_cast<__half *>(y), windows, queries, heads, splits);
   if (dtype == WT_BF16)
     return launch("cross_attn_combine", combine_kernel<__nv_bfloat16>, grid, block, 0, stream, part,
-                  static_cast<__nv_bfloat16 *>(y), queries, heads, splits);
+                  static_cast<__nv_bfloat16 *>(y), windows, queries, heads, splits);
   return fail(WT_ERR_DTYPE, "cross_attn_combine: unknown dtype %d", dtype);
 }
 
