@@ -209,6 +209,9 @@ __global__ void __launch_bounds__(128)
   constexpr int kPass = 8;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   pdl_wait();
+  // the next kernel may launch now: it reads nothing this kernel writes before its own wait, which waits for this
+  // kernel to complete (so a persistent kernel after it issues its first loads while this one runs)
+  pdl_launch_dependents();
   if (idx < static_cast<long long>(W) * H * S * (kD / 8)) {
     const int d8 = static_cast<int>(idx % (kD / 8));
     const long long r = idx / (kD / 8);
@@ -263,7 +266,6 @@ __global__ void __launch_bounds__(128)
     *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + s) * static_cast<size_t>(H) * kD +
                                static_cast<size_t>(h) * kD + 8 * d8) = pack8<T>(num);
   }
-  pdl_launch_dependents();
 }
 
 int query_tiles(int S) {
