@@ -91,6 +91,16 @@ int launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   return WT_OK;
 }
 
+// A launch without the programmatic-dependent-launch attribute whatever the process-wide flag: the kernel starts
+// once its predecessor has completed (its own griddepcontrol.wait is then a no-op), and may still let its successor
+// start early.
+template <typename... KArgs, typename... Args>
+int launch_after(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,
+                 Args... args) {
+  kernel<<<grid, block, smem, static_cast<cudaStream_t>(stream)>>>(static_cast<KArgs>(args)...);
+  return check_launch(what);
+}
+
 // The same with thread-block clusters of `cluster_x` CTAs along x (gridDim.x a multiple of it).
 template <typename... KArgs, typename... Args>
 int launch_clustered(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void *stream,

@@ -377,12 +377,14 @@ int wt_cross_attn_combine(int dtype, const float *part, void *y, int windows, in
   const long long items = static_cast<long long>(windows) * heads * queries * (kD / 8);
   WT_REQUIRE((items + 127) / 128 < (1LL << 31), WT_ERR_ARG, "cross_attn_combine: too large");
   const dim3 grid(static_cast<unsigned>((items + 127) / 128)), block(128);
+  // (after its split, not beside it: early-resident combine CTAs next to the persistent split kernel cost more
+  // than the overlap gains -- measured; it still lets its successor start early)
   if (dtype == WT_F16)
-    return launch("cross_attn_combine", combine_kernel<__half>, grid, block, 0, stream, part,
-                  static_cast<__half *>(y), windows, queries, heads, splits);
+    return launch_after("cross_attn_combine", combine_kernel<__half>, grid, block, 0, stream, part,
+                        static_cast<__half *>(y), windows, queries, heads, splits);
   if (dtype == WT_BF16)
-    return launch("cross_attn_combine", combine_kernel<__nv_bfloat16>, grid, block, 0, stream, part,
-                  static_cast<__nv_bfloat16 *>(y), windows, queries, heads, splits);
+    return launch_after("cross_attn_combine", combine_kernel<__nv_bfloat16>, grid, block, 0, stream, part,
+                        static_cast<__nv_bfloat16 *>(y), windows, queries, heads, splits);
   return fail(WT_ERR_DTYPE, "cross_attn_combine: unknown dtype %d", dtype);
 }
 
