@@ -572,13 +572,23 @@ StreamPlan plan_stream(int W, int S, int H, int Tn, int P) {
     const long long w2 = static_cast<long long>(sm_count()) * kShapes[2].ctas * kShapes[2].warps;
     p.shape = (p.total + w2 - 1) / w2 >= 24 ? (P > 0 ? 3 : 5) : 2;
   }
-  p.grid = sm_count() * kShapes[p.shape].ctas;
-  const long long warps = static_cast<long long>(p.grid) * kShapes[p.shape].warps;
-  p.per_warp = (p.total + warps - 1) / warps;
+  if (P > 0) {
+    // slice mode: one warp per (window, head, slice) unit and as many CTAs as that takes -- the units are small and
+    // equal, so the hardware's CTA scheduling balances them, and no range shares a unit (no partials, no counts):
+    // after the GEMM before it, a persistent grid would pay its ramp and its unit-boundary combines every layer
+    p.per_warp = p.bpu;
+    const long long g = (p.units + kShapes[p.shape].warps - 1) / kShapes[p.shape].warps;
+    p.grid = static_cast<int>(g < (1LL << 31) - 1 ? g : (1LL << 31) - 1);
+  } else {
+    p.grid = sm_count() * kShapes[p.shape].ctas;
+    const long long warps = static_cast<long long>(p.grid) * kShapes[p.shape].warps;
+    p.per_warp = (p.total + warps - 1) / warps;
+  }
   p.max_slots = static_cast<int>((p.bpu + p.per_warp - 1) / p.per_warp + 1);
   p.counters_off = 256;  // [0, 256): the device error word
   p.part_off = p.counters_off + (static_cast<size_t>(p.units) * sizeof(int) + 255) / 256 * 256;
-  p.bytes = p.part_off + static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float);
+  // (slice mode shares no unit between warps: no partials)
+  p.bytes = p.part_off + (P > 0 ? 0 : static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float));
   return p;
 }
 
