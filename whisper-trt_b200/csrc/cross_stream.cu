@@ -29,6 +29,9 @@
 #include "tma.cuh"
 
 namespace wt {
+
+bool cross_stream_slices_ok(int Tn, int P);  // (below)
+
 namespace {
 
 constexpr int kTileBytes = 16 * 128;         // 16 keys x 64 elements x 2 bytes
@@ -62,6 +65,7 @@ struct StreamArgs {
   int *err;
   float *slices_out;  // slice mode: the reference's partials [W, H, P, S, D + 2] instead of y (null: fused output)
   int P, chunk;       // key slices per (window, head) and keys per slice (fused: 1 and Tn)
+  int fuse_slices;    // fused output from slice units: each slice's partial to the workspace, the last one combines
   int W, S, H, Tn, QG, bpu;
   long long total;
   long long per_warp;
@@ -115,8 +119,22 @@ __device__ __forceinline__ void reset_state(State<NT> &st) {
 // The warp's partial for unit u -> workspace (plain stores: nothing waits for them here; the count that publishes
 // them comes later, behind a fence -- see publish() and serve_requests()).
 template <int NT>
+__device__ __forceinline__ void write_record(State<NT> &st, float *dst, int lane);
+template <typename T, int NT>
+__device__ void combine_records(const StreamArgs &a, const float *base, int nslots, const UnitPos &up, int lane);
+
+template <int NT>
 __device__ __forceinline__ void store_partial(State<NT> &st, const StreamArgs &a, long long u, long long gw,
                                               int lane) {
+  const long long fw = first_warp(u, a.bpu, a.per_warp);
+  const int slot = static_cast<int>(gw - fw);
+  write_record<NT>(st, a.part + (static_cast<size_t>(u) * a.max_slots + slot) * (NT * 8) * kPart, lane);
+}
+
+// A warp's online-softmax state -> one record per query of NT * 8 (acc[64], m, l, 2 pad: 16-byte aligned), its
+// row sums first reduced over the lanes that hold them.
+template <int NT>
+__device__ __forceinline__ void write_record(State<NT> &st, float *dst, int lane) {
   const int g = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -124,9 +142,6 @@ __device__ __forceinline__ void store_partial(State<NT> &st, const StreamArgs &a
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) st.l[nt][j] += __shfl_xor_sync(0xffffffffu, st.l[nt][j], o);
-  const long long fw = first_warp(u, a.bpu, a.per_warp);
-  const int slot = static_cast<int>(gw - fw);
-  float *dst = a.part + (static_cast<size_t>(u) * a.max_slots + slot) * (NT * 8) * kPart;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -162,6 +177,21 @@ template <typename T, int NT>
 __device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a, long long u, int lane) {
   const int g = lane >> 2, c = lane & 3;
   const UnitPos p = unit_pos(a, u);
+  if (a.fuse_slices) {  // this slice's record, counted; the (window, head, query group)'s last slice combines
+    const long long grp = (static_cast<long long>(p.w) * a.H + p.h) * a.QG + p.qg;
+    const float *base = a.part + static_cast<size_t>(grp) * a.P * (NT * 8) * kPart;
+    write_record<NT>(st, a.part + (static_cast<size_t>(grp) * a.P + p.sl) * (NT * 8) * kPart, lane);
+    __syncwarp();
+    int old = 0;
+    if (lane == 0)
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + grp) : "memory");
+    if (__shfl_sync(0xffffffffu, old + 1 == a.P ? 1 : 0, 0)) {
+      __syncwarp();
+      combine_records<T, NT>(a, base, a.P, p, lane);
+      if (lane == 0) a.counters[grp] = 0;  // left zeroed for the next launch
+    }
+    return;
+  }
   const int w = p.w, h = p.h, qg = p.qg;
   const size_t HD = static_cast<size_t>(a.H) * kD;
   T *y = static_cast<T *>(a.y);
@@ -202,15 +232,24 @@ __device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a
 // pass by pass.
 constexpr int kCombineSlots = 4;
 template <typename T, int NT>
+__device__ void combine_records(const StreamArgs &a, const float *base, int nslots, const UnitPos &up, int lane);
+
+template <typename T, int NT>
 __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
   __syncwarp();  // (after lane 0's acquire-release count: every lane's loads below are ordered after it)
   const long long fw = first_warp(u, a.bpu, a.per_warp);
   const int nslots = static_cast<int>(last_warp(u, a.bpu, a.per_warp) - fw + 1);
-  const UnitPos up = unit_pos(a, u);
+  combine_records<T, NT>(a, a.part + static_cast<size_t>(u) * a.max_slots * (NT * 8) * kPart, nslots,
+                         unit_pos(a, u), lane);
+  if (lane == 0) a.counters[u] = 0;  // left zeroed for the next launch
+}
+
+// `nslots` records of one (window, head, query group) at `base` -> the output (or, slice mode, the slice's part).
+template <typename T, int NT>
+__device__ void combine_records(const StreamArgs &a, const float *base, int nslots, const UnitPos &up, int lane) {
   const int w = up.w, h = up.h, qg = up.qg;
   const int q0 = qg * NT * 8;
   const int nq = min(NT * 8, a.S - q0);
-  const float *base = a.part + static_cast<size_t>(u) * a.max_slots * (NT * 8) * kPart;
   const size_t HD = static_cast<size_t>(a.H) * kD;
   T *y = static_cast<T *>(a.y);
   constexpr int kItems = NT * 8 * (kD / 8) / 32;  // items per lane (NT * 2)
@@ -294,7 +333,6 @@ __device__ void combine_unit(const StreamArgs &a, long long u, int lane) {
       }
     }
   }
-  if (lane == 0) a.counters[u] = 0;  // left zeroed for the next launch
 }
 
 // The CTA's service warp: lane i waits for streaming warp i's request (its first unit's partial stored, or none),
@@ -545,15 +583,34 @@ int forced_shape() {
 }
 
 struct StreamPlan {
-  int nt, qgs, bpu, max_slots, grid, shape, slices, chunk;
+  int nt, qgs, bpu, max_slots, grid, shape, slices, chunk, fuse;
   long long units, total, per_warp;
   size_t counters_off, part_off, bytes;
 };
 
+// Fused attention of few windows: slice units of ~12 blocks (one wave of warps at most) whose partials the last slice of
+// each (window, head) combines, instead of the persistent stream-K ranges (measured at 8 windows: 12.4 us per launch for
+// the slice units against 15.0). WT_CROSS_FUSE (a tuning knob) forces it on (1) or off (0).
+int fused_slices(int W, int S, int H, int Tn) {
+  static const int forced = [] {  // (read once; a function-local static initialises thread-safely)
+    const char *e = getenv("WT_CROSS_FUSE");
+    return e ? (atoi(e) != 0 ? 1 : 0) : -1;
+  }();
+  if (forced == 0 || S > 8) return 0;
+  const int bpu = (Tn + 15) / 16;
+  const int P = (bpu + 11) / 12;
+  if (P < 2 || !cross_stream_slices_ok(Tn, P)) return 0;
+  const long long resident = static_cast<long long>(sm_count()) * kShapes[2].ctas * kShapes[2].warps;
+  if (forced == 1 || static_cast<long long>(W) * H * P <= resident) return P;
+  return 0;
+}
+
 // P = 0: the fused attention (a unit is a whole (window, head, query group)); P > 0: slice mode, P key slices of
-// ceil(Tn / P) keys per (window, head), each its own unit.
-StreamPlan plan_stream(int W, int S, int H, int Tn, int P) {
+// ceil(Tn / P) keys per (window, head), each its own unit -- with `fuse`, the slices' partials are combined into the
+// output in-kernel instead of written as the reference's part.
+StreamPlan plan_stream(int W, int S, int H, int Tn, int P, bool fuse = false) {
   StreamPlan p{};
+  p.fuse = fuse ? 1 : 0;
   p.nt = (S + 7) / 8 > 4 ? 4 : (S + 7) / 8;
   p.qgs = (S + p.nt * 8 - 1) / (p.nt * 8);
   p.slices = P > 0 ? P : 1;
@@ -587,8 +644,9 @@ StreamPlan plan_stream(int W, int S, int H, int Tn, int P) {
   p.max_slots = static_cast<int>((p.bpu + p.per_warp - 1) / p.per_warp + 1);
   p.counters_off = 256;  // [0, 256): the device error word
   p.part_off = p.counters_off + (static_cast<size_t>(p.units) * sizeof(int) + 255) / 256 * 256;
-  // (slice mode shares no unit between warps: no partials)
-  p.bytes = p.part_off + (P > 0 ? 0 : static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float));
+  // (slice mode shares no unit between warps: no partials; fused from slices, one record per slice)
+  p.bytes = p.part_off + (P > 0 ? (fuse ? static_cast<size_t>(p.units) * p.nt * 8 * kPart * sizeof(float) : 0)
+                                : static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float));
   return p;
 }
 
@@ -627,7 +685,13 @@ int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamA
 
 }  // namespace
 
-size_t cross_stream_workspace(int W, int S, int H, int Tn, int P) { return plan_stream(W, S, H, Tn, P).bytes; }
+size_t cross_stream_workspace(int W, int S, int H, int Tn, int P) {
+  if (P == 0) {
+    const int fp = fused_slices(W, S, H, Tn);
+    if (fp > 0) return plan_stream(W, S, H, Tn, fp, true).bytes;
+  }
+  return plan_stream(W, S, H, Tn, P).bytes;
+}
 
 bool cross_stream_slices_ok(int Tn, int P) {
   // every 16-key block of every slice holds at least one key (the block math needs one)
@@ -638,7 +702,8 @@ bool cross_stream_slices_ok(int Tn, int P) {
 
 int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y, int W, int S, int H, int Tn,
                  void *workspace, size_t workspace_bytes, void *stream, int P, float *slices_out) {
-  const StreamPlan p = plan_stream(W, S, H, Tn, P);
+  const int fp = P == 0 ? fused_slices(W, S, H, Tn) : 0;
+  const StreamPlan p = fp > 0 ? plan_stream(W, S, H, Tn, fp, true) : plan_stream(W, S, H, Tn, P);
   WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,
              "cross_attn: needs a zeroed workspace of %zu bytes (given %zu)", p.bytes, workspace ? workspace_bytes : 0);
   WT_REQUIRE(p.total < (1LL << 40), WT_ERR_ARG, "cross_attn: too large");
@@ -650,7 +715,7 @@ int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y
   if (st != WT_OK) return st;
   char *ws = static_cast<char *>(workspace);
   StreamArgs a{q,       y,    reinterpret_cast<float *>(ws + p.part_off), reinterpret_cast<int *>(ws + p.counters_off),
-               reinterpret_cast<int *>(ws), P > 0 ? slices_out : nullptr, p.slices, p.chunk, W, S, H, Tn, p.qgs,
+               reinterpret_cast<int *>(ws), P > 0 ? slices_out : nullptr, p.slices, p.chunk, p.fuse, W, S, H, Tn, p.qgs,
                p.bpu, p.total, p.per_warp, p.max_slots,
                static_cast<float>(1.0 / 8.0 * 1.4426950408889634), wait_limit(), test_withhold_stage()};
   const bool bf = dtype == WT_BF16;
