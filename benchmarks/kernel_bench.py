@@ -5,6 +5,7 @@ JSON line -- the per-kernel numbers beside bench.py's whole-step line, and the c
     python benchmarks/kernel_bench.py logits32 --rows 160
     python benchmarks/kernel_bench.py prompt --rows 80 --tokens 224 --cached 0
     python benchmarks/kernel_bench.py cross --windows 32 --beams 5
+    python benchmarks/kernel_bench.py cross_split --windows 32 --beams 5
     python benchmarks/kernel_bench.py self_step --rows 160 --cache-lo 4 --cache-hi 224
     python benchmarks/kernel_bench.py dec_linear --rows 160
 
@@ -125,6 +126,30 @@ def cross(a) -> dict:
             "gbs": round(nb / sec / 1e9, 1)}
 
 
+def cross_split(a) -> dict:
+    """The pair the reference's decoder backend calls per layer (runtime.py:144-145): cross_attn_split_triton (the
+    stream-K kernel with (window, head, slice) units) then cross_attn_combine_triton, both timed."""
+    dev, W, K, H, T = "cuda", a.windows, a.beams, 20, 1500
+    g = torch.Generator(device=dev).manual_seed(0)
+    L = max(2, -(-400_000_000 // (W * H * T * 64 * 4)))
+    k = torch.randn(L, W, H, T, 64, generator=g, device=dev).half()
+    v = torch.randn(L, W, H, T, 64, generator=g, device=dev).half()
+    q = torch.randn(L, W, K, H * 64, generator=g, device=dev).half()
+    part = torch.empty(W, H, ap.SPLITS, K, 66, device=dev)
+    out = torch.empty(W, K, H * 64, device=dev, dtype=torch.float16)
+    i = [0]
+
+    def run():
+        j = i[0] % L
+        i[0] += 1
+        ap.cross_attn_combine_triton(ap.cross_attn_split_triton(q[j], k[j], v[j], out=part), q[j], out=out)
+
+    sec = _time(run, a.reps)
+    nb = W * H * T * 64 * 4 + W * K * H * 64 * 4
+    return {"kernel": "cross_attn_split + combine", "windows": W, "queries": K, "us": round(sec * 1e6, 2),
+            "gbs": round(nb / sec / 1e9, 1)}
+
+
 def self_step(a) -> dict:
     dev, N, C, H = "cuda", a.rows, a.capacity, 20
     g = torch.Generator(device=dev).manual_seed(0)
@@ -220,7 +245,8 @@ def dec_linear(a) -> dict:
 
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("kernel", choices=["beam_scores", "logits32", "prompt", "cross", "self_step", "dec_linear"])
+    p.add_argument("kernel", choices=["beam_scores", "logits32", "prompt", "cross", "cross_split", "self_step",
+                                      "dec_linear"])
     p.add_argument("--windows", type=int, default=32)
     p.add_argument("--beams", type=int, default=5)
     p.add_argument("--vocab", type=int, default=51866)
