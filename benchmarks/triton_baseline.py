@@ -346,7 +346,9 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
         variants.append(("ref_triton", "triton", False, False))
     out = {"section": "decoder_step", "workload": name, "rows": N, "windows": W, "capacity": C,
            "cached_mean": round(float(off.float().mean()), 1)}
-    logit_ref = None
+    # every variant captured first (each with its own cache copy and logits), then timed interleaved over `rounds`
+    # rounds -- the median per variant -- so that neither order nor the box's drift favours one
+    graphs, lgs = {}, {}
     for label, gemm, attn, lin in variants:
         try:
             if attn:
@@ -354,18 +356,31 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
             if lin:
                 ours.decoder_kernels.install(RDK)
             backend = RR.TritonDecoderBackend(model, encoder=None, gemm=gemm)
-            cache_v = cache.clone()
-            run = backend.step_fn(tokens, off, cache_v, logits, new_kv, src, cross)
-            t = _time(run, reps)
+            lgs[label] = torch.empty_like(logits)
+            run = backend.step_fn(tokens, off, cache.clone(), lgs[label], new_kv.clone(), src, cross)
+            graphs[label] = _graph(run)
         finally:
             restore()
-        lg = logits.clone()
-        if logit_ref is None:
-            logit_ref = lg
-        out[f"{label}_us"] = round(t * 1e6, 1)
-        out[f"{label}_max_logit_diff_vs_ref_cublas"] = _maxdiff(lg, logit_ref)
-        del cache_v, backend, run
-        torch.cuda.empty_cache()
+    rounds = 5
+    times = {label: [] for label in graphs}
+    for _ in range(rounds):
+        for label, g in graphs.items():
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            times[label].append(e0.elapsed_time(e1) / reps * 1e3)
+    for label in graphs:
+        out[f"{label}_us"] = round(sorted(times[label])[rounds // 2], 1)
+        out[f"{label}_max_logit_diff_vs_ref_cublas"] = _maxdiff(lgs[label], lgs["ref_cublas"])
+    out["timing"] = f"median of {rounds} interleaved rounds of {reps} graph replays per variant"
+    del graphs
+    torch.cuda.empty_cache()
     out["speedup_ours_attn"] = round(out["ref_cublas_us"] / out["ours_attn_us"], 3)
     out["speedup_ours_whole"] = round(out["ref_cublas_us"] / out["ours_whole_us"], 3)
     return out
