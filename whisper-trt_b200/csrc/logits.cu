@@ -2,15 +2,22 @@
 // or bf16 -- the reference's logits32 (attn_plugin.py:202-212 op, :438-455 kernel, :549-560 launcher), the one
 // tensor-core-bound piece next to the attention path.
 //
-// B200 design: 5th-generation tensor cores, one persistent CTA per SM over 128-entry vocabulary tiles (x 256-row
-// chunks of x): a tile's rows of w are the MMA's A (M = 128), the rows of x its B (N = the rows, padded to 16), the
-// reduction d in 64-element blocks staged by TMA (128-byte swizzle) through a ring of up to 8 stages. Warp 0's lane
-// 0 issues the TMA loads, warp 1's lane 0 the tcgen05.mma instructions (kind::f16, fp32 accumulator in tensor
-// memory, two accumulators in turn); a stage is released by a tcgen05.commit on its "empty" barrier when its MMAs
-// complete, an accumulator by a commit on its "full" barrier. Warps 2-5 read the accumulator's 128 lanes
-// (vocabulary entries) with tcgen05.ld, 16 rows at a time, store them as consecutive floats of each output row and
-// hand the accumulator back -- under the next tile's loads and MMAs. Every barrier wait is bounded (a timeout
-// records an error in the device word and the kernel goes on, then frees its tensor memory).
+// B200 design: 5th-generation tensor cores. The work is cut into items of G 128-entry vocabulary tiles x one chunk of
+// up to 256 rows of x; a tile's rows of w are the MMA's A (M = 128), the chunk's rows of x its B (N = the rows, padded
+// to 16), the reduction d in 64-element blocks staged by TMA (128-byte swizzle) through a ring. One stage holds the
+// item's G w blocks and ONE x block: the G tiles share each x block (x is read from L2 once per item, not once per
+// tile), and G is the smallest group that fits every item in one wave over the SMs (160 rows x 51866 entries: 406
+// tiles in 136 items of 3 on 148 SMs), so no SM idles through a last partial wave. G accumulators of N fp32 columns
+// sit side by side in tensor memory (two sets in turn when they fit twice in its 512 columns).
+//   * warp 0's lane 0 issues the TMA loads -- the first stages' w blocks before the wait for the preceding kernel
+//     (w is not its output), their x blocks after it; warp 1's lane 0 issues the tcgen05.mma instructions (kind::f16,
+//     fp32 accumulators in tensor memory) and releases a stage with a tcgen05.commit on its "empty" barrier;
+//   * warps 2-9 drain the accumulators (each warp its lane quarter, warp % 4, and every other 16-column slice), store
+//     them as consecutive floats of each output row and hand the set back;
+//   * every barrier wait is bounded (a timeout records an error in the device word and the kernel goes on, then
+//     frees its tensor memory).
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -21,38 +28,82 @@
 namespace wt {
 namespace {
 
-constexpr int kLgEpiWarps = 4;
-constexpr int kLgThreads = 32 * (2 + kLgEpiWarps);  // producer, MMA issuer, 4 epilogue warps
-constexpr int kLgTileV = 128;   // vocabulary entries per CTA (the MMA's M)
-constexpr int kLgKBlock = 64;   // reduction elements per stage (one 128-byte swizzled row)
-constexpr int kLgMaxRows = 256; // rows of x per CTA (the MMA's N, at most 256)
+constexpr int kLgEpiWarps = 8;
+constexpr int kLgThreads = 32 * (2 + kLgEpiWarps);  // producer, MMA issuer, 8 epilogue warps
+constexpr int kLgTileV = 128;    // vocabulary entries per tile (the MMA's M)
+constexpr int kLgKBlock = 64;    // reduction elements per stage (one 128-byte swizzled row)
+constexpr int kLgMaxRows = 256;  // rows of x per chunk (the MMA's N, at most 256)
+constexpr int kLgMaxGroup = 4;   // vocabulary tiles per item
+constexpr int kLgTmemCols = 512;
+constexpr int kLgSmemBudget = 216 * 1024;  // the ring (one CTA per SM)
 constexpr int kLgErrTimeout = 1;
 
-// Persistent: CTA c takes tiles c, c + grid, ... (tile = vocabulary tile x row chunk). Warp 0 (lane 0) streams
-// the tiles' k-blocks through the ring, warp 1 (lane 0) issues their MMAs into one of two tensor-memory
-// accumulators, warps 2-5 drain the other one (each warp its lane quarter, warp % 4), so a tile's epilogue runs
-// under the next tile's loads and MMAs.
+struct LgPlan {
+  int chunks, nmma, stride, vtiles, group, items, nbuf, tcols, kblocks, stage_bytes, stages, smem, grid;
+};
+
+// Vocabulary tiles per item forced by WT_LG_GROUP (a tuning knob, 1-4), else 0 (chosen by the plan).
+int lg_group() {
+  static const int v = [] {  // (read once; a function-local static initialises thread-safely)
+    const char *e = getenv("WT_LG_GROUP");
+    const int x = e ? atoi(e) : 0;
+    return (x >= 1 && x <= kLgMaxGroup) ? x : 0;
+  }();
+  return v;
+}
+
+int lg_stage_bytes(int group, int nmma) { return group * kLgTileV * 128 + (nmma * 128 + 1023) / 1024 * 1024; }
+
+LgPlan lg_plan(int rows, int vocab, int d_model, int sms) {
+  LgPlan p{};
+  p.chunks = (rows + kLgMaxRows - 1) / kLgMaxRows;
+  p.nmma = ((rows + p.chunks - 1) / p.chunks + 15) / 16 * 16;  // balanced chunks
+  p.stride = (p.nmma + 31) / 32 * 32;                           // tensor-memory columns per accumulator
+  p.vtiles = (vocab + kLgTileV - 1) / kLgTileV;
+  p.kblocks = (d_model + kLgKBlock - 1) / kLgKBlock;
+  int gmax = kLgTmemCols / p.stride;
+  if (gmax > kLgMaxGroup) gmax = kLgMaxGroup;
+  while (gmax > 1 && 2 * lg_stage_bytes(gmax, p.nmma) > kLgSmemBudget) --gmax;  // at least two stages
+  p.group = gmax;
+  for (int g = 1; g <= gmax; ++g)  // the smallest group whose items all fit one wave
+    if (static_cast<long long>(p.chunks) * ((p.vtiles + g - 1) / g) <= sms) {
+      p.group = g;
+      break;
+    }
+  if (lg_group() > 0 && lg_group() <= gmax) p.group = lg_group();
+  p.items = p.chunks * ((p.vtiles + p.group - 1) / p.group);
+  p.nbuf = 2 * p.group * p.stride <= kLgTmemCols ? 2 : 1;
+  p.tcols = 32;
+  while (p.tcols < p.nbuf * p.group * p.stride) p.tcols <<= 1;
+  p.stage_bytes = lg_stage_bytes(p.group, p.nmma);
+  p.stages = kLgSmemBudget / p.stage_bytes;
+  if (p.stages > 8) p.stages = 8;
+  p.smem = 1024 + p.stages * p.stage_bytes + (2 * p.stages + 4) * 8 + 16;
+  p.grid = p.items < sms ? p.items : sms;
+  return p;
+}
+
+// Persistent: CTA c takes items c, c + grid, ...; item i is (vocabulary group i / chunks, row chunk i % chunks), so
+// the CTAs that share a group's w run side by side and the later chunks find it in L2.
 template <bool BF16>
 __global__ void __launch_bounds__(kLgThreads)
     logits_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                  float *__restrict__ y, int N, int V, int kblocks, int nmma, int tcols, int stages, int *err,
-                  uint32_t polls) {
+                  float *__restrict__ y, int N, int V, const LgPlan p, int *err, uint32_t polls) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int a_bytes = kLgTileV * 128, b_bytes = nmma * 128;
-  const int stage_bytes = a_bytes + ((b_bytes + 1023) & ~1023);
+  constexpr int a_bytes = kLgTileV * 128;
+  const int G = p.group, stages = p.stages, stage_bytes = p.stage_bytes, kblocks = p.kblocks, nmma = p.nmma;
+  const int b_bytes = nmma * 128;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + stages * stage_bytes);
   uint64_t *empty = full + stages;
   uint64_t *acc_full = empty + stages;
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_empty + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int vtiles = (V + kLgTileV - 1) / kLgTileV;
-  const int tiles = vtiles * ((N + kLgMaxRows - 1) / kLgMaxRows);
 
   if (warp == 0) {
-    tmem_alloc(tmem_holder, static_cast<uint32_t>(2 * tcols));
+    tmem_alloc(tmem_holder, static_cast<uint32_t>(p.tcols));
     tmem_relinquish();
   }
   if (tid == 32) {
@@ -73,65 +124,106 @@ __global__ void __launch_bounds__(kLgThreads)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  pdl_wait();
-  pdl_launch_dependents();
-
   if (warp == 0) {
-    if (lane == 0) {  // producer: every k-block of every tile of this CTA, through the ring
+    if (lane == 0) {  // producer: every k block of every item of this CTA, through the ring
+      // the first item's first stage: its w blocks before the wait for the preceding kernel, its x block after it
+      // (one stage: the x block the first MMAs need then waits behind no more w than that; measured faster alone)
+      const int pre = static_cast<int>(blockIdx.x) < p.items ? 1 : 0;
       int it = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int v0 = (t % vtiles) * kLgTileV, n0 = (t / vtiles) * kLgMaxRows;
+      for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
+        const int t0 = (item / p.chunks) * G, n0 = (item % p.chunks) * nmma;
+        const int ng = min(G, p.vtiles - t0);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % stages;
-          if (it >= stages) mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1, err, kLgErrTimeout, polls);
           unsigned char *st = smem + s * stage_bytes;
-          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(a_bytes + b_bytes));
-          tma_load_2d(st, &wmap, kb * kLgKBlock, v0, &full[s]);
-          tma_load_2d(st + a_bytes, &xmap, kb * kLgKBlock, n0, &full[s]);
+          if (it < pre) {
+            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ng * a_bytes + b_bytes));
+            for (int g = 0; g < ng; ++g) tma_load_2d(st + g * a_bytes, &wmap, kb * kLgKBlock, (t0 + g) * kLgTileV, &full[s]);
+            if (it == pre - 1) {
+              pdl_wait();
+              pdl_launch_dependents();
+              for (int j = 0; j < pre; ++j)
+                tma_load_2d(smem + j * stage_bytes + G * a_bytes, &xmap, j * kLgKBlock, n0, &full[j]);
+            }
+            continue;
+          }
+          if (it >= stages) mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1, err, kLgErrTimeout, polls);
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ng * a_bytes + b_bytes));
+          tma_load_2d(st + G * a_bytes, &xmap, kb * kLgKBlock, n0, &full[s]);  // (x first: it is in L2)
+          for (int g = 0; g < ng; ++g) tma_load_2d(st + g * a_bytes, &wmap, kb * kLgKBlock, (t0 + g) * kLgTileV, &full[s]);
         }
       }
+      if (pre == 0) {
+        pdl_wait();
+        pdl_launch_dependents();
+      }
+    } else {
+      pdl_wait();
+      pdl_launch_dependents();
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer: tile j into accumulator j % 2 once the epilogue has drained it
+    pdl_wait();
+    pdl_launch_dependents();
+    if (lane == 0) {  // MMA issuer: item j into accumulator set j % nbuf once the epilogue has drained it
       const uint32_t idesc = idesc_f16(kLgTileV, nmma, BF16);
       int it = 0, j = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
-        const int b = j & 1;
-        if (j >= 2) mbar_wait_bounded(&acc_empty[b], ((j >> 1) - 1) & 1, err, kLgErrTimeout, polls);
+      for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++j) {
+        const int ng = min(G, p.vtiles - (item / p.chunks) * G);
+        const int b = j % p.nbuf, use = j / p.nbuf;
+        if (use >= 1) mbar_wait_bounded(&acc_empty[b], (use - 1) & 1, err, kLgErrTimeout, polls);
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(b * tcols);
+        const uint32_t d = tmem + static_cast<uint32_t>(b * G * p.stride);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % stages;
           mbar_wait_bounded(&full[s], (it / stages) & 1, err, kLgErrTimeout, polls);
           tc_fence_after();
-          const uint32_t a_addr = smem_addr(smem + s * stage_bytes), b_addr = a_addr + a_bytes;
-          const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(b_addr);
+          const uint32_t a_addr = smem_addr(smem + s * stage_bytes);
+          const uint64_t bdesc = sw128_desc(a_addr + static_cast<uint32_t>(G * a_bytes));
+          for (int g = 0; g < ng; ++g) {
+            const uint64_t adesc = sw128_desc(a_addr + static_cast<uint32_t>(g * a_bytes));
+            const uint32_t dg = d + static_cast<uint32_t>(g * p.stride);
 #pragma unroll
-          for (int kk = 0; kk < kLgKBlock / 16; ++kk)  // K = 16 per instruction: +32 bytes along the swizzled row
-            umma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+            for (int kk = 0; kk < kLgKBlock / 16; ++kk)  // K = 16 per instruction: +32 bytes along the swizzled row
+              umma_f16(dg, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          }
           umma_commit(&empty[s]);
         }
         umma_commit(&acc_full[b]);
       }
     }
-  } else {  // epilogue warps: lane quarter warp % 4 = vocabulary entries v0 + 32 (warp % 4) + lane
-    const int quarter = warp & 3;
+  } else {  // epilogue warps: lane quarter warp % 4 (vocabulary entries 32 (warp % 4) + lane of each tile), and
+            // the 16-column slices c0 = 16 half, 16 half + 32, ... of the rows
+    pdl_wait();
+    pdl_launch_dependents();
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     int j = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
-      const int b = j & 1;
-      const int v = (t % vtiles) * kLgTileV + quarter * 32 + lane, n0 = (t / vtiles) * kLgMaxRows;
-      mbar_wait_bounded(&acc_full[b], (j >> 1) & 1, err, kLgErrTimeout, polls);
+    for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++j) {
+      const int t0 = (item / p.chunks) * G, n0 = (item % p.chunks) * nmma;
+      const int ng = min(G, p.vtiles - t0);
+      const int b = j % p.nbuf, use = j / p.nbuf;
+      mbar_wait_bounded(&acc_full[b], use & 1, err, kLgErrTimeout, polls);
       tc_fence_after();
-      const uint32_t base = tmem + static_cast<uint32_t>(b * tcols) + (static_cast<uint32_t>(quarter * 32) << 16);
-      for (int c0 = 0; c0 < nmma; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(base + static_cast<uint32_t>(c0), r);
-        tmem_wait_ld();
-        if (v < V) {
+      for (int g = 0; g < ng; ++g) {
+        const int v = (t0 + g) * kLgTileV + quarter * 32 + lane;
+        const uint32_t base = tmem + static_cast<uint32_t>((b * G + g) * p.stride) +
+                              (static_cast<uint32_t>(quarter * 32) << 16);
+        // four 16-column slices per wait: the tensor-memory loads' latency is paid once per 64 values
+        for (int cb = 16 * half; cb < nmma; cb += 128) {
+          uint32_t r[4][16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const int n = n0 + c0 + q;
-            if (n < N) y[static_cast<size_t>(n) * V + v] = __uint_as_float(r[q]);
+          for (int q = 0; q < 4; ++q)
+            if (cb + 32 * q < nmma) tmem_ld16(base + static_cast<uint32_t>(cb + 32 * q), r[q]);
+          tmem_wait_ld();
+          if (v < V) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (cb + 32 * q >= nmma) break;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int n = n0 + cb + 32 * q + i;
+                if (n < N) y[static_cast<size_t>(n) * V + v] = __uint_as_float(r[q][i]);
+              }
+            }
           }
         }
       }
@@ -143,7 +235,7 @@ __global__ void __launch_bounds__(kLgThreads)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(2 * tcols));
+  if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(p.tcols));
 }
 
 }  // namespace
@@ -160,30 +252,20 @@ extern "C" int wt_logits32(int dtype, const void *x, const void *w, float *y, in
   WT_ALIGNED(y);
   WT_REQUIRE(d_model % 8 == 0, WT_ERR_UNSUPPORTED, "logits32: d_model %d is not a multiple of 8", d_model);
   WT_REQUIRE(dtype == WT_F16 || dtype == WT_BF16, WT_ERR_DTYPE, "logits32: unknown dtype %d", dtype);
-  const int chunks = (rows + kLgMaxRows - 1) / kLgMaxRows;
-  const int nrows = rows < kLgMaxRows ? rows : kLgMaxRows;
-  const int nmma = (nrows + 15) / 16 * 16;
-  int tcols = 32;
-  while (tcols < nmma) tcols <<= 1;
+  const int sms = device_sm_count();
+  if (sms <= 0) return WT_ERR_CUDA;
+  const LgPlan p = lg_plan(rows, vocab, d_model, sms);
   CUtensorMap wm, xm;
   int st = encode_tile_map(&wm, w, static_cast<unsigned long long>(vocab), static_cast<unsigned long long>(d_model),
                            kLgTileV, dtype);
   if (st != WT_OK) return st;
-  st = encode_tile_map(&xm, x, static_cast<unsigned long long>(rows), static_cast<unsigned long long>(d_model), nmma,
-                       dtype);
+  st = encode_tile_map(&xm, x, static_cast<unsigned long long>(rows), static_cast<unsigned long long>(d_model),
+                       p.nmma, dtype);
   if (st != WT_OK) return st;
-  const int stage_bytes = kLgTileV * 128 + (nmma * 128 + 1023) / 1024 * 1024;
-  const int stages = (200 * 1024) / stage_bytes < 8 ? (200 * 1024) / stage_bytes : 8;  // one CTA per SM
-  const int smem = 1024 + stages * stage_bytes + (2 * stages + 4) * 8 + 16;
-  const int kblocks = (d_model + kLgKBlock - 1) / kLgKBlock;
   auto kernel = dtype == WT_BF16 ? logits_kernel<true> : logits_kernel<false>;
-  st = dtype == WT_BF16 ? opt_in_smem<logits_kernel<true>>(smem, "logits32")
-                        : opt_in_smem<logits_kernel<false>>(smem, "logits32");
+  st = dtype == WT_BF16 ? opt_in_smem<logits_kernel<true>>(p.smem, "logits32")
+                        : opt_in_smem<logits_kernel<false>>(p.smem, "logits32");
   if (st != WT_OK) return st;
-  const int sms = device_sm_count();
-  if (sms <= 0) return WT_ERR_CUDA;
-  const int tiles = ((vocab + kLgTileV - 1) / kLgTileV) * chunks;
-  const int grid = tiles < sms ? tiles : sms;
-  return launch("logits32", kernel, dim3(grid), dim3(kLgThreads), smem, stream, wm, xm, y, rows, vocab, kblocks,
-                nmma, tcols, stages, err, wait_limit());
+  return launch("logits32", kernel, dim3(p.grid), dim3(kLgThreads), p.smem, stream, wm, xm, y, rows, vocab, p, err,
+                wait_limit());
 }

@@ -8,10 +8,9 @@ namespace wt {
 namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
-}  // namespace
 
-int encode_tile_map(CUtensorMap *map, const void *base, unsigned long long rows, unsigned long long cols,
-                    int box_rows, int dtype) {
+int encode_map(CUtensorMap *map, const void *base, unsigned long long rows, unsigned long long cols, int box_cols,
+               int box_rows, bool swizzle, int dtype) {
   std::call_once(g_encode_once, [] {
     void *fn = nullptr;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
@@ -23,14 +22,21 @@ int encode_tile_map(CUtensorMap *map, const void *base, unsigned long long rows,
   if (g_encode == nullptr) return fail(WT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
-  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t elem[2] = {1, 1};
   const CUresult r =
       g_encode(map, dtype == WT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                const_cast<void *>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+               swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(WT_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
   return WT_OK;
+}
+}  // namespace
+
+int encode_tile_map(CUtensorMap *map, const void *base, unsigned long long rows, unsigned long long cols,
+                    int box_rows, int dtype) {
+  return encode_map(map, base, rows, cols, 64, box_rows, true, dtype);
 }
 
 int encode_rows128_map(CUtensorMap *map, const void *base, unsigned long long rows, int box_rows, int dtype) {
