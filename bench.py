@@ -13,8 +13,8 @@ several GB, far more than the 126 MB L2, so no flush is needed between steps.
 
 value = algorithmic HBM bytes per step (see ``step_bytes``) x steps / time, summed over all GPUs (GB/s, whole job);
 ms_per_step = the max over ranks of the device time per step. Prints one JSON line on rank 0, with: ``e2e`` (the
-same step through the public API with its inputs copied in from pinned host memory and its outputs copied out, and
-the copy rate each rank gets); ``roofline`` (the dominant kernel's achieved bandwidth); ``also`` (configs 2, 4 and
+same step through the public API with its inputs copied in from pinned host memory and its result -- the last
+layer's outputs -- copied out, and the copy rate each rank gets); ``roofline`` (the dominant kernel's achieved bandwidth); ``also`` (configs 2, 4 and
 5 at the same N); at N = 1 ``vs_reference_gpu`` (the reference's own Triton kernels timed beside these on the same
 inputs) and ``cpu_baseline``.
 
@@ -550,23 +550,26 @@ def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, 
 
 def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_state, sch, warmup,
             dist=None) -> dict:
-    """The step through the public API with its inputs copied in from pinned host memory and its outputs copied
+    """The step through the public API with its inputs copied in from pinned host memory and its result copied
     out every step; whole-job GB/s (bytes summed over ranks, time the max).
 
     The inputs are each layer's qkv and cross queries and the step's schedule row (parents, window replacements),
-    which the host writes into pinned staging before each step. One CUDA graph per step: a copy-in stream brings
-    the layers' inputs in order, the compute stream runs layer i once its inputs have landed, and a copy-out stream
-    takes layer i's outputs back while layer i + 1 runs, so the PCIe transfers overlap the HBM-bound kernels. Two
-    steps are in flight, as a serving loop keeps them: the host stages step s + 1's schedule row while step s runs
-    (two pinned staging and output buffers, one graph for each) and reads each step's outputs once that step's
-    completion event has fired, one step behind; nothing of a step's copies is skipped."""
+    which the host writes into pinned staging before each step. The step's result is its last layer's attention
+    outputs (self and cross), which the host reads back: the earlier layers' outputs feed the next layer on the
+    device in a decoder and never cross PCIe (copying them all out too added 26 MB a step per rank, which 8 ranks
+    sharing the host's links could not move in a step's time). One CUDA graph per step: a copy-in stream brings the
+    layers' inputs in order, the compute stream runs layer i once its inputs have landed, so the PCIe transfers
+    overlap the HBM-bound kernels, and a copy-out stream takes the last layer's outputs back. Two steps are in
+    flight, as a serving loop keeps them: the host stages step s + 1's schedule row while step s runs (two pinned
+    staging and output buffers, one graph for each) and reads each step's result once that step's completion event
+    has fired, one step behind; nothing of a step's copies is skipped."""
     W, K = sch.W, sch.K
     qkv_h = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
     q_h = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     qkv_h.copy_(qkv)
     q_h.copy_(q)
-    ys_h = [torch.empty(y_self.shape, dtype=y_self.dtype, pin_memory=True) for _ in range(2)]
-    yc_h = [torch.empty(y_cross.shape, dtype=y_cross.dtype, pin_memory=True) for _ in range(2)]
+    ys_h = [torch.empty(y_self.shape[1:], dtype=y_self.dtype, pin_memory=True) for _ in range(2)]
+    yc_h = [torch.empty(y_cross.shape[1:], dtype=y_cross.dtype, pin_memory=True) for _ in range(2)]
     stage = [{k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in cur.items()} for _ in range(2)]
     arange_w = np.arange(W)
 
@@ -581,7 +584,7 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
     n = qkv.shape[0]
     cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(n)]
-    ev_out = [torch.cuda.Event() for _ in range(n)]
+    ev_out = torch.cuda.Event()
     ev_sched = torch.cuda.Event()
 
     def piped_step(b: int):
@@ -599,11 +602,11 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
         for i in range(n):
             main.wait_event(ev_in[i])
             layer(i)
-            ev_out[i].record(main)
-            cout.wait_event(ev_out[i])
-            with torch.cuda.stream(cout):
-                ys_h[b][i].copy_(y_self[i], non_blocking=True)
-                yc_h[b][i].copy_(y_cross[i], non_blocking=True)
+        ev_out.record(main)
+        cout.wait_event(ev_out)
+        with torch.cuda.stream(cout):  # the step's result: the last layer's outputs
+            ys_h[b].copy_(y_self[n - 1], non_blocking=True)
+            yc_h[b].copy_(y_cross[n - 1], non_blocking=True)
         main.wait_event(ev_sched)
         tail()
         main.wait_stream(cin)
@@ -627,13 +630,13 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
             b = s % 2
             if s - 2 >= first:
                 done[b].synchronize()  # step s - 2 (this buffer's last user) is complete: read its result
-                checksum[0] += float(ys_h[b][-1, 0, 0, 0]) + float(yc_h[b][-1, 0, 0, 0])
+                checksum[0] += float(ys_h[b][0, 0, 0]) + float(yc_h[b][0, 0, 0])
             fill_stage(b, s)
             graphs[b].replay()
             done[b].record(stream)
         for s in range(max(first, first + count - 2), first + count):  # the last two steps' results
             done[s % 2].synchronize()
-            checksum[0] += float(ys_h[s % 2][-1, 0, 0, 0]) + float(yc_h[s % 2][-1, 0, 0, 0])
+            checksum[0] += float(ys_h[s % 2][0, 0, 0]) + float(yc_h[s % 2][0, 0, 0])
 
     run(0, warmup)
     if dist:
@@ -647,7 +650,7 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
     ms, nbytes = combine_ranks(ev0.elapsed_time(ev1), sum(sch.step_bytes(s) for s in range(warmup, warmup + steps)),
                                dist, dev)
     h2d = sum(t.numel() * t.element_size() for t in (qkv, q, *cur.values()))
-    d2h = y_self.numel() * y_self.element_size() + y_cross.numel() * y_cross.element_size()
+    d2h = sum(t.numel() * t.element_size() for t in (ys_h[0], yc_h[0]))
     del graphs
     # the copy-in alone (the layers' qkv and queries, 3 steps' worth), every rank at once after a barrier: the
     # pinned host-to-device rate each rank gets when all copy together -- the bound of the step above when the
@@ -677,9 +680,10 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
                                 "(slowest rank): the bound on the e2e step"},
             "path": "whisper_trt_b200.attn_plugin calls (C ABI) captured in a CUDA graph; every step the host "
                     "stages the step's schedule row, the layers' qkv / queries and the schedule are copied in from "
-                    "pinned host memory and the layers' outputs copied out (per layer, on copy streams that overlap "
-                    "the compute stream); two steps in flight: the host stages step s + 1 while step s runs and "
-                    "reads each step's outputs when its completion event fires"}
+                    "pinned host memory (per layer, on a copy stream that overlaps the compute stream) and the "
+                    "step's result (the last layer's self and cross outputs) copied out; two steps in flight: the "
+                    "host stages step s + 1 while step s runs and reads each step's result when its completion "
+                    "event fires"}
 
 
 # --- the reference's CPU implementation ---------------------------------------------------------------------------
