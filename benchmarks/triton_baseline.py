@@ -347,8 +347,10 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
     out = {"section": "decoder_step", "workload": name, "rows": N, "windows": W, "capacity": C,
            "cached_mean": round(float(off.float().mean()), 1)}
     # every variant captured first (each with its own cache copy and logits), then timed interleaved over `rounds`
-    # rounds -- the median per variant -- so that neither order nor the box's drift favours one
-    graphs, lgs = {}, {}
+    # rounds -- the median per variant -- so that neither order nor the box's drift favours one. Each variant's step
+    # closure (and with it its backend, cache copy and concatenated weights) is kept for as long as its graph: a
+    # capture begins with torch.cuda.empty_cache(), which would unmap a dropped variant's buffers under its graph.
+    graphs, lgs, alive = {}, {}, {}
     for label, gemm, attn, lin in variants:
         try:
             if attn:
@@ -358,6 +360,7 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
             backend = RR.TritonDecoderBackend(model, encoder=None, gemm=gemm)
             lgs[label] = torch.empty_like(logits)
             run = backend.step_fn(tokens, off, cache.clone(), lgs[label], new_kv.clone(), src, cross)
+            alive[label] = (backend, run)
             graphs[label] = _graph(run)
         finally:
             restore()
@@ -380,6 +383,7 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
         out[f"{label}_max_logit_diff_vs_ref_cublas"] = _maxdiff(lgs[label], lgs["ref_cublas"])
     out["timing"] = f"median of {rounds} interleaved rounds of {reps} graph replays per variant"
     del graphs
+    del alive
     torch.cuda.empty_cache()
     out["speedup_ours_attn"] = round(out["ref_cublas_us"] / out["ours_attn_us"], 3)
     out["speedup_ours_whole"] = round(out["ref_cublas_us"] / out["ours_whole_us"], 3)

@@ -119,7 +119,9 @@ int wt_self_attn(int dtype, const void *qkv, const void *k_cache, const void *v_
  *   wt_cross_attn_workspace() bytes, with the same per-shape rule as wt_self_attn_step's: zeroed before its
  *   first use with a shape, valid for further calls of that shape only, not shared by calls that may overlap.
  *   Its first 4 bytes are a device error word: non-zero after a kernel's bounded wait for its own TMA copies gave
- *   up (the output is then not valid); the kernel never hangs. The size depends on the device's SM count.
+ *   up (the output is then not valid); the kernel never hangs. With at most 8 queries per window (one CTA per
+ *   (window, head), its key slices combined on chip) the workspace is that word alone (256 bytes); larger query
+ *   groups take the stream-K kernel, whose size depends on the device's SM count.
  * ------------------------------------------------------------------------------------------------------- */
 int wt_cross_attn_split(int dtype, const void *q, const void *k, const void *v, float *part, int windows,
                         int queries, int heads, int frames, int head_dim, int splits, void *stream);

@@ -96,7 +96,8 @@ def test_workspace_sizes():
     lib = _lib.load()
     assert lib.wt_self_attn_step_workspace(40, 20, 64, 1) == 0
     assert lib.wt_self_attn_step_workspace(5, 20, 64, 4) >= 5 * 20 * 4 * 66 * 4
-    assert lib.wt_cross_attn_workspace(8, 5, 20, 1500, 64) > 8 * 20 * 66 * 4
+    assert lib.wt_cross_attn_workspace(8, 5, 20, 1500, 64) == 256  # one CTA per (window, head): the error word only
+    assert lib.wt_cross_attn_workspace(8, 16, 20, 1500, 64) > 8 * 20 * 66 * 4  # stream-K: partials and counters
     assert lib.wt_cross_attn_workspace(8, 5, 20, 1500, 32) == 0
 
 

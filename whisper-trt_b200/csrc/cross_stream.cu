@@ -1,9 +1,11 @@
-// Fused cross-attention (split + combine in one launch) as a persistent, stream-K balanced kernel fed by TMA.
+// Fused cross-attention (split + combine in one launch), fed by TMA: a window of at most 8 queries (a beam or a
+// sample group) takes cross_window_kernel below -- one CTA per (window, head), 8 key slices combined in shared
+// memory; larger query groups, and the reference-shaped split (slice mode), take the persistent stream-K kernel.
 //
 // Semantics: the reference's cross_attn (attn_plugin.py:129-136, kernel :352-376) -- softmax(q k^T / sqrt(D)) v per
 // (window, head) over the window's T encoder frames, scores in log2 units; fp32 accumulation.
 //
-// B200 design. The work is the flat sequence of (window, head, query group, 16-key block) units -- 94 blocks per
+// The stream-K kernel. The work is the flat sequence of (window, head, query group, 16-key block) units -- 94 blocks per
 // (window, head) at T = 1500 -- cut into one equal contiguous range per streaming warp of a persistent grid
 // ("stream-K": every warp streams the same number of bytes, no wave tail whatever the window count):
 //   * each streaming warp owns a ring of stages in shared memory; its lane 0 issues 2D TMA loads (16 rows x 128 bytes
@@ -565,6 +567,142 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   }
 }
 
+// Fused attention of few windows, one CTA per (window, head): its kWinSlices warps each stream one key slice of the
+// window's frames through their own TMA ring (16-key blocks, two at a time), and the slices' online-softmax states
+// meet in shared memory after a CTA barrier, where 8 threads per query combine them into the output. No partial
+// leaves the SM and no counter is taken: the tail after the last block is a few hundred cycles (the stream-K and
+// slice-unit kernels end with a partial's stores, a GPU-scope count and an L2 round trip per combined slice). With
+// programmatic dependent launch the first stages' loads go out before the wait for the preceding kernel.
+constexpr int kWinSlices = 8;
+constexpr int kWinStages = 3;
+constexpr int kWinRing = kWinStages * kStageBytes;
+constexpr int kWinSmem = kWinSlices * kWinRing + kWinSlices * kWinStages * 8 + 1024;
+
+template <typename T>
+__global__ void __launch_bounds__(kWinSlices * 32, 2)
+    cross_window_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        const T *__restrict__ q, T *__restrict__ y, int *err, int S, int H, int Tn, int chunk,
+                        float scale, uint32_t polls, int withhold) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int wh = blockIdx.x, w = wh / H, h = wh - (wh / H) * H;
+  unsigned char *ring = smem + warp * kWinRing;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWinSlices * kWinRing) + warp * kWinStages;
+  const int k_lo = warp * chunk;
+  const int klen = max(0, min(Tn - k_lo, chunk));  // keys of this warp's slice
+  const int nblk = (klen + 15) / 16;
+  if (lane == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+#pragma unroll
+    for (int s = 0; s < kWinStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const int row0 = wh * Tn + k_lo;
+  // (the bounded-wait test hook: warp 0 of CTA 0 issues nothing for its first block, whose wait then runs out)
+  const bool hold = withhold && wh == 0 && warp == 0;
+  auto issue = [&](int b) {  // lane 0: block b of the slice into its stage
+    const int s = b % kWinStages;
+    unsigned char *dst = ring + s * kStageBytes;
+    if (hold && b == 0) return;
+    mbar_arrive_expect_tx(&bars[s], kStageBytes);
+    tma_load_2d(dst, &kmap, 0, row0 + b * 16, &bars[s]);
+    tma_load_2d(dst + kTileBytes, &vmap, 0, row0 + b * 16, &bars[s]);
+  };
+  if (lane == 0)
+    for (int b = 0; b < min(nblk, kWinStages); ++b) issue(b);
+  // (the cross keys/values are not the preceding kernel's output; the queries and the output wait for it)
+  pdl_wait();
+  pdl_launch_dependents();
+
+  const size_t HD = static_cast<size_t>(H) * kD;
+  uint32_t qf[1][8];
+  load_q_std<T, 1>(qf, q + static_cast<size_t>(w) * S * HD + static_cast<size_t>(h) * kD, HD, 0, S, g, c);
+  State<1> st;
+  reset_state<1>(st);
+  uint32_t late = 0;  // stages whose wait timed out (their copies may still be in flight)
+  for (int j = 0; j < nblk;) {
+    const bool pair = j + 1 < nblk;
+    const int s0 = j % kWinStages;
+    if (!mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kWinStages) & 1), err, kErrTimeout, polls))
+      late |= 1u << s0;
+    uint32_t ka[4][4], va[4][4];
+    smem_frags(ka, va, ring + s0 * kStageBytes, ring + s0 * kStageBytes + kTileBytes, lane);
+    const int k0 = j * 16;
+    if (pair) {
+      const int s1 = (j + 1) % kWinStages;
+      if (!mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kWinStages) & 1), err, kErrTimeout, polls))
+        late |= 1u << s1;
+      uint32_t kb[4][4], vb[4][4];
+      smem_frags(kb, vb, ring + s1 * kStageBytes, ring + s1 * kStageBytes + kTileBytes, lane);
+      consume_frags(ka, va);
+      consume_frags(kb, vb);
+      __syncwarp();
+      if (lane == 0) {  // both stages' operands are in registers: refill them
+        if (j + kWinStages < nblk) issue(j + kWinStages);
+        if (j + 1 + kWinStages < nblk) issue(j + 1 + kWinStages);
+      }
+      const bool ok[2][2] = {{k0 + g < klen, k0 + g + 8 < klen}, {k0 + 16 + g < klen, k0 + 24 + g < klen}};
+      attend_block2<T, 1>(st, ka, va, kb, vb, qf, ok, scale);
+      j += 2;
+    } else {
+      consume_frags(ka, va);
+      __syncwarp();
+      if (lane == 0 && j + kWinStages < nblk) issue(j + kWinStages);
+      attend_block<T, 1>(st, ka, va, qf, k0 + g < klen, k0 + g + 8 < klen, scale);
+      j += 1;
+    }
+  }
+  // this slice's state (acc, m, l per query) over the start of its ring: every stage has been consumed (a timed-out
+  // stage's copy may still land there -- the output is invalid then, and the error word says so)
+  __syncwarp();
+  float *rec = reinterpret_cast<float *>(ring);
+  if (late == 0) write_record<1>(st, rec, lane);
+  __syncthreads();
+  // the slices' states -> the output: thread t takes query t / 8, head dims 8 (t % 8) .. + 7 (attn_plugin.py:182-194)
+  for (int t = threadIdx.x; t < S * 8; t += blockDim.x) {
+    const int qq = t >> 3, d8 = t & 7;
+    float top = kNegInf;
+#pragma unroll
+    for (int sl = 0; sl < kWinSlices; ++sl) {
+      const float *r = reinterpret_cast<const float *>(smem + sl * kWinRing) + qq * kPart;
+      top = fmaxf(top, r[kD]);
+    }
+    float den = 0.f, num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int sl = 0; sl < kWinSlices; ++sl) {
+      const float *r = reinterpret_cast<const float *>(smem + sl * kWinRing) + qq * kPart;
+      const float ms = r[kD];
+      const float wgt = ms == kNegInf ? 0.f : ex2(ms - top);
+      den = fmaf(wgt, r[kD + 1], den);
+      const float4 x = *reinterpret_cast<const float4 *>(r + 8 * d8), z = *reinterpret_cast<const float4 *>(r + 8 * d8 + 4);
+      num[0] = fmaf(wgt, x.x, num[0]);
+      num[1] = fmaf(wgt, x.y, num[1]);
+      num[2] = fmaf(wgt, x.z, num[2]);
+      num[3] = fmaf(wgt, x.w, num[3]);
+      num[4] = fmaf(wgt, z.x, num[4]);
+      num[5] = fmaf(wgt, z.y, num[5]);
+      num[6] = fmaf(wgt, z.z, num[6]);
+      num[7] = fmaf(wgt, z.w, num[7]);
+    }
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) num[i] *= inv;
+    *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + qq) * HD + static_cast<size_t>(h) * kD + 8 * d8) =
+        pack8<T>(num);
+  }
+  // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
+  for (int j = nblk - min(nblk, kWinStages); j < nblk; ++j) {
+    const int s = j % kWinStages;
+    if (late & (1u << s))
+      mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kWinStages) & 1), nullptr, 0, polls);
+  }
+}
+
 // The SM count the plan is sized for (148 on a B200 if the device cannot be queried: the launch then reports the
 // device's own error).
 int sm_count() {
@@ -603,6 +741,19 @@ int fused_slices(int W, int S, int H, int Tn) {
   const long long resident = static_cast<long long>(sm_count()) * kShapes[2].ctas * kShapes[2].warps;
   if (forced == 1 || static_cast<long long>(W) * H * P <= resident) return P;
   return 0;
+}
+
+// The one-CTA-per-(window, head) kernel takes the fused attention when a window has at most 8 queries (one query
+// tile) and every 16-key block of the 8 slices holds a key; the stream-K kernel the rest. Measured per launch, chained
+// as in the step (stream-K -> this kernel): 8 windows 14.3 -> 13.3 us, 32 windows 44.2 -> 43.7 us, 64 windows 91.6 ->
+// 78.1 us (the CTAs' dynamic scheduling leaves a smaller tail than the stream-K ranges' unit-boundary combines).
+// WT_CROSS_WINDOW=0 (a tuning knob) turns it off.
+bool window_kernel_ok(int W, int S, int H, int Tn) {
+  static const int off = [] {  // (read once; a function-local static initialises thread-safely)
+    const char *e = getenv("WT_CROSS_WINDOW");
+    return (e != nullptr && atoi(e) == 0) ? 1 : 0;
+  }();
+  return !off && W > 0 && H > 0 && S <= 8 && cross_stream_slices_ok(Tn, kWinSlices);
 }
 
 // P = 0: the fused attention (a unit is a whole (window, head, query group)); P > 0: slice mode, P key slices of
@@ -686,6 +837,7 @@ int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamA
 }  // namespace
 
 size_t cross_stream_workspace(int W, int S, int H, int Tn, int P) {
+  if (P == 0 && window_kernel_ok(W, S, H, Tn)) return 256;  // (the device error word only)
   if (P == 0) {
     const int fp = fused_slices(W, S, H, Tn);
     if (fp > 0) return plan_stream(W, S, H, Tn, fp, true).bytes;
@@ -702,6 +854,32 @@ bool cross_stream_slices_ok(int Tn, int P) {
 
 int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y, int W, int S, int H, int Tn,
                  void *workspace, size_t workspace_bytes, void *stream, int P, float *slices_out) {
+  if (P == 0 && window_kernel_ok(W, S, H, Tn)) {
+    WT_REQUIRE(static_cast<long long>(W) * H * Tn < (1LL << 31), WT_ERR_ARG, "cross_attn: too large");
+    WT_REQUIRE(workspace && workspace_bytes >= 256, WT_ERR_WORKSPACE,
+               "cross_attn: needs a zeroed workspace of 256 bytes (given %zu)", workspace ? workspace_bytes : 0);
+    CUtensorMap km, vm;
+    const unsigned long long rows = static_cast<unsigned long long>(W) * H * Tn;
+    int st = encode_rows128_map(&km, k, rows, 16, dtype);
+    if (st != WT_OK) return st;
+    st = encode_rows128_map(&vm, v, rows, 16, dtype);
+    if (st != WT_OK) return st;
+    const int chunk = (Tn + kWinSlices - 1) / kWinSlices;
+    const float scale = static_cast<float>(1.0 / 8.0 * 1.4426950408889634);
+    int *err = static_cast<int *>(workspace);
+    if (dtype == WT_BF16) {
+      st = opt_in_smem<cross_window_kernel<__nv_bfloat16>>(kWinSmem, "cross_attn");
+      if (st != WT_OK) return st;
+      return launch("cross_attn", cross_window_kernel<__nv_bfloat16>, dim3(W * H), dim3(kWinSlices * 32), kWinSmem,
+                    stream, km, vm, static_cast<const __nv_bfloat16 *>(q), static_cast<__nv_bfloat16 *>(y), err, S,
+                    H, Tn, chunk, scale, wait_limit(), test_withhold_stage());
+    }
+    st = opt_in_smem<cross_window_kernel<__half>>(kWinSmem, "cross_attn");
+    if (st != WT_OK) return st;
+    return launch("cross_attn", cross_window_kernel<__half>, dim3(W * H), dim3(kWinSlices * 32), kWinSmem, stream,
+                  km, vm, static_cast<const __half *>(q), static_cast<__half *>(y), err, S, H, Tn, chunk, scale,
+                  wait_limit(), test_withhold_stage());
+  }
   const int fp = P == 0 ? fused_slices(W, S, H, Tn) : 0;
   const StreamPlan p = fp > 0 ? plan_stream(W, S, H, Tn, fp, true) : plan_stream(W, S, H, Tn, P);
   WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,

@@ -11,14 +11,13 @@
 //     (so no key load waits on an index load) and its warps take 4 contiguous quarters of the keys, so the longest
 //     row's chain of dependent loads is a quarter as long as with one warp per (row, head), and the many short
 //     CTAs balance over the SMs by themselves;
-//   * each warp streams stages of 4 * U keys through an S-deep cp.async ring (16-byte copies, bypassing L1; head_dim
-//     64 with up to 256 slots per split: U = 2, S = 3, 24 KB of rings per CTA keep 8 CTAs on an SM; else U = 4,
-//     S = 2): the loads in
-//     flight hold no registers, and the ring is laid out chunk-major ([chunk][lane]) so every read-back is bank-
-//     conflict free;
-//   * a key row is covered by D/8 lanes (one 16-byte piece each), dot products on mixed-precision FMAs (half/bf16
-//     products accumulated in fp32) finished with butterfly shuffles; each group of D/8 lanes runs its own online
-//     softmax (U keys per stage); groups merge by shuffles, the 4 warps through shared memory;
+//   * each warp streams stages of (32 / LPK) * U keys through an S-deep cp.async ring (16-byte copies, bypassing
+//     L1; head_dim 64 with up to 256 slots per split: U = 2, S = 3, 24 KB of rings per CTA keep 8 CTAs on an SM;
+//     else U = 4, S = 2): the loads in flight hold no registers, and the ring is laid out piece-major
+//     ([piece][lane]) so every read-back is bank-conflict free;
+//   * a key row is covered by LPK lanes (D/8 by default: one 16-byte piece each), dot products on mixed-precision
+//     FMAs (half/bf16 products accumulated in fp32) finished with butterfly shuffles; each group of LPK lanes runs
+//     its own online softmax (U keys per stage); groups merge by shuffles, the 4 warps through shared memory;
 //   * kv_splits > 1 splits the cache capacity into equal static ranges; each split writes its partial (acc, m, l)
 //     to the workspace and the last CTA of the (row, head) -- an atomic counter, no waiting -- combines them;
 //   * with programmatic dependent launch the offset, slot table and cache reads start before the preceding kernel
@@ -91,30 +90,36 @@ __device__ __forceinline__ float group_sum(float x) {
 }
 
 // Merge two online-softmax states (m, l, acc) -> first.
-__device__ __forceinline__ void merge_state(float &m, float &l, float (&acc)[8], float m2, float l2,
-                                            const float (&acc2)[8]) {
+template <int NA>
+__device__ __forceinline__ void merge_state(float &m, float &l, float (&acc)[NA], float m2, float l2,
+                                            const float (&acc2)[NA]) {
   const float mn = fmaxf(m, m2);
   const float mu = (mn == kNegInf) ? 0.f : mn;
   const float a1 = ex2(m - mu), a2 = ex2(m2 - mu);
   l = l * a1 + l2 * a2;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = acc[i] * a1 + acc2[i] * a2;
+  for (int i = 0; i < NA; ++i) acc[i] = acc[i] * a1 + acc2[i] * a2;
   m = mn;
 }
 
-// shared memory: per warp a ring ([stage][2 * U chunks][32 lanes] x 16 bytes), then the CTA's staged source rows
-template <int U, int S>
-constexpr int ring_bytes() { return S * 2 * U * 32 * 16; }
+// shared memory: per warp a ring ([stage][2 * U * CPL pieces][32 lanes] x 16 bytes), then the CTA's staged source rows
+template <int U, int CPL, int S>
+constexpr int ring_bytes() { return S * 2 * U * CPL * 32 * 16; }
 
-template <typename T, int D, int U, int kStages>
+// LPK lanes cover a key row, CPL 16-byte pieces each: piece c of lane sub holds head dims (c * LPK + sub) * 8 .. + 7,
+// so one copy instruction of the warp reads LPK contiguous pieces (whole 32-byte sectors) of each of its key rows.
+template <typename T, int D, int LPK, int U, int kStages>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
     self_step_kernel(const T *__restrict__ qkv, T *kc, T *vc, const int64_t *__restrict__ offset,
                      const int32_t *__restrict__ src, T *__restrict__ y, float *__restrict__ part,
                      int *__restrict__ counters, int N, int H, int C, int write_cache, int splits, float scale) {
-  constexpr int LPK = D / 8;     // lanes per key row (16 bytes each)
-  constexpr int GPW = 32 / LPK;  // key groups per warp
-  constexpr int kRingBytes = ring_bytes<U, kStages>();
-  constexpr int KPS = GPW * U;   // keys per stage
+  constexpr int CPL = D / (8 * LPK);  // 16-byte pieces per lane of a key row
+  constexpr int NA = 8 * CPL;         // head dims per lane
+  constexpr int GPW = 32 / LPK;       // key groups per warp
+  constexpr int kStageBytes = 2 * U * CPL * 32 * 16;
+  constexpr int kRingBytes = ring_bytes<U, CPL, kStages>();
+  constexpr int KPS = GPW * U;        // keys per stage
+  static_assert(D % (8 * LPK) == 0 && 32 % LPK == 0, "lanes per key must tile the head dim and the warp");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = blockIdx.x / H, h = blockIdx.x - (blockIdx.x / H) * H;
@@ -148,16 +153,20 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   const size_t row_stride = static_cast<size_t>(H) * C * D;
   const T *kh = kc + static_cast<size_t>(h) * C * D + sub * 8;
   const T *vh = vc + static_cast<size_t>(h) * C * D + sub * 8;
-  // stage t: this lane's keys wlo + t*KPS + grp*U + u; piece i (K: u, V: U + u) at ring[t % S][i][lane]
+  // stage t: this lane's keys wlo + t*KPS + grp*U + u; piece (u, c) of K at ring[t % S][u * CPL + c][lane], of V at
+  // ring[t % S][(U + u) * CPL + c][lane]
   auto issue = [&](int t) {
-    unsigned char *slot = ring + (t % kStages) * (2 * U * 32 * 16);
+    unsigned char *slot = ring + (t % kStages) * kStageBytes;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = wlo + t * KPS + grp * U + u;
       if (j < whi) {
         const size_t o = static_cast<size_t>(rows_s[j - lo]) * row_stride + static_cast<size_t>(j) * D;
-        cp_async16(slot + (u * 32 + lane) * 16, kh + o);
-        cp_async16(slot + ((U + u) * 32 + lane) * 16, vh + o);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          cp_async16(slot + ((u * CPL + c) * 32 + lane) * 16, kh + o + c * LPK * 8);
+          cp_async16(slot + (((U + u) * CPL + c) * 32 + lane) * 16, vh + o + c * LPK * 8);
+        }
       }
     }
   };
@@ -172,30 +181,48 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   // this kernel to complete
   pdl_launch_dependents();
   const T *qrow = qkv + static_cast<size_t>(r) * 3 * HD + static_cast<size_t>(h) * D + sub * 8;
-  const uint4 qraw = ldg16(qrow);
-  const uint32_t qw[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
+  uint32_t qw[4 * CPL];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) {
+    const uint4 qraw = ldg16(qrow + c * LPK * 8);
+    qw[4 * c] = qraw.x;
+    qw[4 * c + 1] = qraw.y;
+    qw[4 * c + 2] = qraw.z;
+    qw[4 * c + 3] = qraw.w;
+  }
   // the new token first: every row attends to it (attn_plugin.py:331-334); group 0 of warp 0 of split 0 owns it
   const bool owner = sp == 0 && warp == 0;
-  float m = kNegInf, l = 0.f, acc[8];
+  float m = kNegInf, l = 0.f, acc[NA];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int i = 0; i < NA; ++i) acc[i] = 0.f;
   if (owner) {
-    const uint4 kraw = ldg16(qrow + HD), vraw = ldg16(qrow + 2 * HD);
-    if (write_cache && grp == 0 && off < C) {
-      const size_t own = ((static_cast<size_t>(r) * H + h) * C + off) * D + sub * 8;
-      *reinterpret_cast<uint4 *>(kc + own) = kraw;
-      *reinterpret_cast<uint4 *>(vc + own) = vraw;
-    }
     float s_new = 0.f;
-    s_new = MixFma<T>::dot2(qw[0], kraw.x, s_new);
-    s_new = MixFma<T>::dot2(qw[1], kraw.y, s_new);
-    s_new = MixFma<T>::dot2(qw[2], kraw.z, s_new);
-    s_new = MixFma<T>::dot2(qw[3], kraw.w, s_new);
+    uint4 vraw[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const uint4 kraw = ldg16(qrow + HD + c * LPK * 8);
+      vraw[c] = ldg16(qrow + 2 * HD + c * LPK * 8);
+      if (write_cache && grp == 0 && off < C) {
+        const size_t own = ((static_cast<size_t>(r) * H + h) * C + off) * D + sub * 8 + c * LPK * 8;
+        *reinterpret_cast<uint4 *>(kc + own) = kraw;
+        *reinterpret_cast<uint4 *>(vc + own) = vraw[c];
+      }
+      s_new = MixFma<T>::dot2(qw[4 * c], kraw.x, s_new);
+      s_new = MixFma<T>::dot2(qw[4 * c + 1], kraw.y, s_new);
+      s_new = MixFma<T>::dot2(qw[4 * c + 2], kraw.z, s_new);
+      s_new = MixFma<T>::dot2(qw[4 * c + 3], kraw.w, s_new);
+    }
     s_new = group_sum<LPK>(s_new) * scale;  // (the scale after the dot product, as attn_plugin.py:332)
     if (grp == 0) {
       m = s_new;
       l = 1.f;
-      unpack8<T>(vraw, acc);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        float vf[8];
+        unpack8<T>(vraw[c], vf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[8 * c + i] = vf[i];
+      }
     }
   }
 
@@ -203,18 +230,21 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     if (t + kStages - 1 < nst) issue(t + kStages - 1);
     cp_async_commit();
     cp_async_wait<kStages - 1>();  // stage t has landed (this lane's copies)
-    const unsigned char *slot = ring + (t % kStages) * (2 * U * 32 * 16);
+    const unsigned char *slot = ring + (t % kStages) * kStageBytes;
     float s[U];
     bool ok[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       ok[u] = wlo + t * KPS + grp * U + u < whi;
-      const uint4 kw = *reinterpret_cast<const uint4 *>(slot + (u * 32 + lane) * 16);
       float a = 0.f;
-      a = MixFma<T>::dot2(qw[0], kw.x, a);
-      a = MixFma<T>::dot2(qw[1], kw.y, a);
-      a = MixFma<T>::dot2(qw[2], kw.z, a);
-      a = MixFma<T>::dot2(qw[3], kw.w, a);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const uint4 kw = *reinterpret_cast<const uint4 *>(slot + ((u * CPL + c) * 32 + lane) * 16);
+        a = MixFma<T>::dot2(qw[4 * c], kw.x, a);
+        a = MixFma<T>::dot2(qw[4 * c + 1], kw.y, a);
+        a = MixFma<T>::dot2(qw[4 * c + 2], kw.z, a);
+        a = MixFma<T>::dot2(qw[4 * c + 3], kw.w, a);
+      }
       s[u] = a;
     }
 #pragma unroll
@@ -230,16 +260,19 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
     const float alpha = ex2(m - mu);
     l *= alpha;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] *= alpha;
+    for (int i = 0; i < NA; ++i) acc[i] *= alpha;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (ok[u]) {  // (a key past the range was never copied: its bytes are stale)
         const float p = ex2(s[u] - mu);
         l += p;
-        float vf[8];
-        unpack8<T>(*reinterpret_cast<const uint4 *>(slot + ((U + u) * 32 + lane) * 16), vf);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = fmaf(p, vf[i], acc[i]);
+        for (int c = 0; c < CPL; ++c) {
+          float vf[8];
+          unpack8<T>(*reinterpret_cast<const uint4 *>(slot + (((U + u) * CPL + c) * 32 + lane) * 16), vf);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[8 * c + i] = fmaf(p, vf[i], acc[8 * c + i]);
+        }
       }
     }
     m = mn;
@@ -250,9 +283,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
 #pragma unroll
   for (int o = LPK; o < 32; o <<= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
-    float acc2[8];
+    float acc2[NA];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc2[i] = __shfl_xor_sync(0xffffffffu, acc[i], o);
+    for (int i = 0; i < NA; ++i) acc2[i] = __shfl_xor_sync(0xffffffffu, acc[i], o);
     merge_state(m, l, acc, m2, l2, acc2);
   }
   __syncthreads();
@@ -260,7 +293,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   if (grp == 0) {
     float *mine = st_s + warp * (D + 2);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mine[sub * 8 + i] = acc[i];
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mine[(c * LPK + sub) * 8 + i] = acc[8 * c + i];
     if (sub == 0) {
       mine[D] = m;
       mine[D + 1] = l;
@@ -271,9 +306,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
 #pragma unroll
   for (int w2 = 1; w2 < kWarpsPerCta; ++w2) {
     const float *other = st_s + w2 * (D + 2);
-    float acc2[8];
+    float acc2[NA];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc2[i] = other[sub * 8 + i];
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc2[8 * c + i] = other[(c * LPK + sub) * 8 + i];
     merge_state(m, l, acc, other[D], other[D + 1], acc2);
   }
   const int rh = r * H + h;
@@ -281,14 +318,20 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   if (splits == 1) {
     const float inv = 1.f / l;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] *= inv;
-    *reinterpret_cast<uint4 *>(yo) = pack8<T>(acc);
+    for (int c = 0; c < CPL; ++c) {
+      float o8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = acc[8 * c + i] * inv;
+      *reinterpret_cast<uint4 *>(yo + c * LPK * 8) = pack8<T>(o8);
+    }
     return;
   }
   // the last split of this (row, head) to finish combines the partials (lanes 0 .. LPK-1 of warp 0)
   float *pp = part + (static_cast<size_t>(rh) * splits + sp) * (D + 2);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) pp[sub * 8 + i] = acc[i];
+  for (int c = 0; c < CPL; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pp[(c * LPK + sub) * 8 + i] = acc[8 * c + i];
   if (sub == 0) {
     pp[D] = m;
     pp[D + 1] = l;
@@ -303,19 +346,27 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   const float *pr = part + static_cast<size_t>(rh) * splits * (D + 2);
   float top = kNegInf;
   for (int s2 = 0; s2 < splits; ++s2) top = fmaxf(top, __ldcg(pr + s2 * (D + 2) + D));
-  float num[8] = {0, 0, 0, 0, 0, 0, 0, 0}, den = 0.f;
+  float num[NA], den = 0.f;
+#pragma unroll
+  for (int i = 0; i < NA; ++i) num[i] = 0.f;
   for (int s2 = 0; s2 < splits; ++s2) {
     const float *p2 = pr + s2 * (D + 2);
     const float ms = __ldcg(p2 + D);
     const float wgt = (ms == kNegInf) ? 0.f : ex2(ms - top);
     den = fmaf(wgt, __ldcg(p2 + D + 1), den);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) num[i] = fmaf(wgt, __ldcg(p2 + sub * 8 + i), num[i]);
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) num[8 * c + i] = fmaf(wgt, __ldcg(p2 + (c * LPK + sub) * 8 + i), num[8 * c + i]);
   }
   const float inv = 1.f / den;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) num[i] *= inv;
-  *reinterpret_cast<uint4 *>(yo) = pack8<T>(num);
+  for (int c = 0; c < CPL; ++c) {
+    float o8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o8[i] = num[8 * c + i] * inv;
+    *reinterpret_cast<uint4 *>(yo + c * LPK * 8) = pack8<T>(o8);
+  }
   if (sub == 0) counters[rh] = 0;  // left zeroed for the next launch
 }
 
@@ -325,13 +376,13 @@ size_t step_workspace(int rows, int heads, int head_dim, int splits) {
   return counters + static_cast<size_t>(rows) * heads * splits * (head_dim + 2) * sizeof(float);
 }
 
-template <typename T, int D, int U, int kStages>
+template <typename T, int D, int LPK, int U, int kStages>
 int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y, int N,
                 int H, int C, int write_cache, int splits, void *ws, void *stream) {
   const int cap = (C + splits - 1) / splits;
-  const int smem = kWarpsPerCta * ring_bytes<U, kStages>() + (cap * 4 + 15) / 16 * 16;
-  auto kernel = self_step_kernel<T, D, U, kStages>;
-  const int st = opt_in_smem<self_step_kernel<T, D, U, kStages>>(smem, "self_attn_step");
+  const int smem = kWarpsPerCta * ring_bytes<U, D / (8 * LPK), kStages>() + (cap * 4 + 15) / 16 * 16;
+  auto kernel = self_step_kernel<T, D, LPK, U, kStages>;
+  const int st = opt_in_smem<self_step_kernel<T, D, LPK, U, kStages>>(smem, "self_attn_step");
   if (st != WT_OK) return st;
   int *counters = nullptr;
   float *part = nullptr;
@@ -346,17 +397,19 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
                 static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale);
 }
 
-// Ring shape (keys per lane group per stage, stages) of the head_dim 64 kernel. By default it follows the cache
-// slots per split: up to 256, (2, 3) -- 24 KB of rings per CTA keep 8 CTAs on an SM while 16 keys per warp are in
-// flight before the wait for the preceding kernel (measured per step: 1980 -> 1924 us at 160 rows, C 228; 670 ->
-// 666 us at 40 rows); above, (4, 2) -- long rows want 32 keys per warp in flight (1589 us at 80 rows, C 448, lengths
-// U[224, 447], against 1674 with (2, 3)). WT_SELF_SHAPE (a tuning knob) forces 0 = (4, 2), 1 = (2, 2), 2 = (2, 3) or
-// 3 = (1, 4).
+// Shape (lanes per key row, keys per lane group per stage, stages) of the head_dim 64 kernel. By default it follows
+// the cache slots per split: up to 256, (8, 2, 3) -- 24 KB of rings per CTA keep 8 CTAs on an SM while 16 keys per
+// warp are in flight before the wait for the preceding kernel (measured per step: 1980 -> 1924 us at 160 rows, C
+// 228; 670 -> 666 us at 40 rows); above, (8, 4, 2) -- long rows want 32 keys per warp in flight (1589 us at 80 rows,
+// C 448, lengths U[224, 447], against 1674 with (8, 2, 3)). Four lanes per key row with two 16-byte pieces each,
+// (4, 1, 3), time the same at 160 rows, C 228 (18.6 us per launch chained; (4, 2, 2) 20.3, (4, 2, 3) 23.6 and
+// (2, 1, 2) 29.5): the kernel is bound by its loads' latency, not by the shuffles and FMAs per key. WT_SELF_SHAPE (a
+// tuning knob) forces 0 = (8, 4, 2), 1 = (8, 2, 2), 2 = (8, 2, 3), 3 = (8, 1, 4) or 4 = (4, 1, 3).
 int self_shape(int cap) {
   static const int forced = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_SELF_SHAPE");
     const int x = e ? atoi(e) : -1;
-    return (x >= 0 && x <= 3) ? x : -1;
+    return (x >= 0 && x <= 4) ? x : -1;
   }();
   if (forced >= 0) return forced;
   return cap <= 256 ? 2 : 0;
@@ -365,19 +418,23 @@ int self_shape(int cap) {
 template <typename T>
 int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y,
                   int N, int H, int C, int write_cache, int splits, void *ws, void *stream) {
+#define WT_STEP(D_, LPK_, U_, S_) \
+  launch_step<T, D_, LPK_, U_, S_>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream)
   switch (D) {
-    case 16: return launch_step<T, 16, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-    case 32: return launch_step<T, 32, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+    case 16: return WT_STEP(16, 2, 4, 2);
+    case 32: return WT_STEP(32, 4, 4, 2);
     case 64:
       switch (self_shape((C + splits - 1) / splits)) {
-        case 1: return launch_step<T, 64, 2, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-        case 3: return launch_step<T, 64, 1, 4>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-        case 2: return launch_step<T, 64, 2, 3>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
-        default: return launch_step<T, 64, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+        case 1: return WT_STEP(64, 8, 2, 2);
+        case 2: return WT_STEP(64, 8, 2, 3);
+        case 3: return WT_STEP(64, 8, 1, 4);
+        case 4: return WT_STEP(64, 4, 1, 3);
+        default: return WT_STEP(64, 8, 4, 2);
       }
-    case 128: return launch_step<T, 128, 4, 2>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream);
+    case 128: return WT_STEP(128, 16, 4, 2);
     default: return fail(WT_ERR_UNSUPPORTED, "self_attn_step: head_dim %d (supported: 16, 32, 64, 128)", D);
   }
+#undef WT_STEP
 }
 
 }  // namespace
