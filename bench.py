@@ -428,7 +428,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) 
         "data": DATA,
         "config": make_config(args, wl, Schedule(wl, n_sched, shard_seed(0), start=args.warmup), world),
         "frac_of_hbm_peak": round(value / world / peak, 4), "hbm_peak_gbs": peak, "hbm_peak_kind": peak_kind,
-        "roofline": {"bound": "hbm", "kernel": "cross_attn (fused split + combine)",
+        "roofline": {"bound": "hbm", "kernel": "cross_attn (cross_window_kernel: split + combine fused, one CTA per (window, head))",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": cross_bytes, "launch_us": round(ker["cross_ms"] * 1e3, 2),
