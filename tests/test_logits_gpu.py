@@ -29,7 +29,8 @@ def _check(x, w, y):
 
 @pytest.mark.parametrize("rows,vocab,d", [(160, 51866, 1280), (40, 51866, 1280), (1, 1000, 1280), (5, 129, 1280),
                                           (16, 128, 64), (17, 300, 384), (300, 2000, 512), (256, 640, 1280),
-                                          (320, 51866, 1280), (600, 2000, 256)])
+                                          (320, 51866, 1280), (600, 2000, 256), (160, 51865, 1280),
+                                          (7, 301, 256)])
 def test_shapes(rows, vocab, d):
     x, w = _case(rows, vocab, d)
     y = ap.logits32_triton(x, w)

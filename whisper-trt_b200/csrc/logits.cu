@@ -207,22 +207,43 @@ __global__ void __launch_bounds__(kLgThreads)
         const int v = (t0 + g) * kLgTileV + quarter * 32 + lane;
         const uint32_t base = tmem + static_cast<uint32_t>((b * G + g) * p.stride) +
                               (static_cast<uint32_t>(quarter * 32) << 16);
-        // four 16-column slices per wait: the tensor-memory loads' latency is paid once per 64 values
+        // four 16-column slices per wait. With V even, lanes 2j and 2j + 1 (entries v, v + 1) swap half their rows
+        // so that each stores 8-byte pairs (every row of y then starts 8-byte aligned): the even lane rows i, the odd
+        // lane rows 8 + i of each slice -- one store instruction covers two rows; with V odd, one float per store
+        const int vp = v & ~1;
+        const bool odd = (lane & 1) != 0;
         for (int cb = 16 * half; cb < nmma; cb += 128) {
           uint32_t r[4][16];
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             if (cb + 32 * q < nmma) tmem_ld16(base + static_cast<uint32_t>(cb + 32 * q), r[q]);
           tmem_wait_ld();
-          if (v < V) {
+          if (V & 1) {
+            if (v < V) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              if (cb + 32 * q >= nmma) break;
+              for (int q = 0; q < 4; ++q) {
+                if (cb + 32 * q >= nmma) break;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int n = n0 + cb + 32 * q + i;
-                if (n < N) y[static_cast<size_t>(n) * V + v] = __uint_as_float(r[q][i]);
+                for (int i = 0; i < 16; ++i) {
+                  const int n = n0 + cb + 32 * q + i;
+                  if (n < N) y[static_cast<size_t>(n) * V + v] = __uint_as_float(r[q][i]);
+                }
               }
+            }
+            continue;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (cb + 32 * q >= nmma) break;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t mine = odd ? r[q][8 + i] : r[q][i];
+              const uint32_t other = __shfl_xor_sync(0xffffffffu, odd ? r[q][i] : r[q][8 + i], 1);
+              const int n = n0 + cb + 32 * q + (odd ? 8 + i : i);
+              if (n < N && vp < V)  // (V even: v + 1 < V too)
+                *reinterpret_cast<float2 *>(y + static_cast<size_t>(n) * V + vp) =
+                    odd ? make_float2(__uint_as_float(other), __uint_as_float(mine))
+                        : make_float2(__uint_as_float(mine), __uint_as_float(other));
             }
           }
         }
