@@ -870,7 +870,8 @@ def run_reference_gpu(local_rank: int, reps: int = 10) -> dict:
     out["how"] = ("device time per step of CUDA-graph replays (10 after 3 warm-up), the same seeded inputs and static "
                   "offsets on both sides; attention alone (no bookkeeping), and decoder_step: the whole 32-layer decode "
                   "step through the reference's own TritonDecoderBackend (random-init whisper-large-v3 decoder), as it "
-                  "ships (ref_cublas) and with this package installed (ours_attn: attention + logits32; ours_whole: "
+                  "ships (ref_cublas) and with this package installed (ours_attn: attention + logits32; ours_attn_ln: also its "
+                  "LayerNorms, the GEMMs still cuBLAS; ours_whole: "
                   "also the fused linear layers); the reference's Triton 3.6 kernels from baseline/_ref")
     return out
 

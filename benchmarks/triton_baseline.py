@@ -303,6 +303,8 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
     * ``ref_cublas``: the reference as it ships (its Triton attention and LayerNorm kernels, cuBLAS GEMMs, its
       logits32 kernel);
     * ``ours_attn``: the same backend with this package installed into its ``attn_plugin`` (attention, logits32);
+    * ``ours_attn_ln``: the same, and this package's ``decoder_kernels`` installed too -- in the cuBLAS step that
+      routes the three LayerNorms per layer (``layer_norm_bias``) to this package; the GEMMs stay cuBLAS;
     * ``ours_whole``: its ``gemm="triton"`` variant with this package installed into ``attn_plugin`` and
       ``decoder_kernels``: every kernel of the step but the embedding gather, the final LayerNorm and one cast;
     * ``ref_triton`` (with ``ref_gemm_triton``): the reference's own ``gemm="triton"`` variant (autotunes first).
@@ -341,7 +343,7 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
                 setattr(m, k, v)
 
     variants = [("ref_cublas", "cublas", False, False), ("ours_attn", "cublas", True, False),
-                ("ours_whole", "triton", True, True)]
+                ("ours_attn_ln", "cublas", True, True), ("ours_whole", "triton", True, True)]
     if ref_gemm_triton:
         variants.append(("ref_triton", "triton", False, False))
     out = {"section": "decoder_step", "workload": name, "rows": N, "windows": W, "capacity": C,
@@ -386,6 +388,7 @@ def decoder_step(R, ours, name: str, reps: int, ref_gemm_triton: bool = False) -
     del alive
     torch.cuda.empty_cache()
     out["speedup_ours_attn"] = round(out["ref_cublas_us"] / out["ours_attn_us"], 3)
+    out["speedup_ours_attn_ln"] = round(out["ref_cublas_us"] / out["ours_attn_ln_us"], 3)
     out["speedup_ours_whole"] = round(out["ref_cublas_us"] / out["ours_whole_us"], 3)
     return out
 

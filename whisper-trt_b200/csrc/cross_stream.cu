@@ -573,16 +573,22 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
 // leaves the SM and no counter is taken: the tail after the last block is a few hundred cycles (the stream-K and
 // slice-unit kernels end with a partial's stores, a GPU-scope count and an L2 round trip per combined slice). With
 // programmatic dependent launch the first stages' loads go out before the wait for the preceding kernel.
-constexpr int kWinSlices = 8;
-constexpr int kWinStages = 3;
-constexpr int kWinRing = kWinStages * kStageBytes;
-constexpr int kWinSmem = kWinSlices * kWinRing + kWinSlices * kWinStages * 8 + 1024;
+// Shapes (slices = warps per CTA, ring stages per warp, CTAs per SM); WT_CROSS_WIN_SHAPE (a tuning knob) picks one.
+// Measured per launch chained at 32 windows (config 2 / config 5 step): (8, 3, 2) 44.3 us (572 / 4516 us); (16, 2, 1)
+// 45.3 (661 / 4633); (16, 3, 1) 46.2 (678 / 4743); (12, 3, 1) 46.2 (668 / 4776) -- finer slices do not pay for the
+// single CTA per SM.
+struct WinShape {
+  int slices, stages, ctas;
+};
+constexpr WinShape kWinShapes[] = {{8, 3, 2}, {16, 2, 1}};
+constexpr int win_smem(int slices, int stages) { return slices * stages * kStageBytes + slices * stages * 8 + 1024; }
 
-template <typename T>
-__global__ void __launch_bounds__(kWinSlices * 32, 2)
+template <typename T, int kWinSlices, int kWinStages, int kWinCtas>
+__global__ void __launch_bounds__(kWinSlices * 32, kWinCtas)
     cross_window_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                         const T *__restrict__ q, T *__restrict__ y, int *err, int S, int H, int Tn, int chunk,
                         float scale, uint32_t polls, int withhold) {
+  constexpr int kWinRing = kWinStages * kStageBytes;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -748,12 +754,51 @@ int fused_slices(int W, int S, int H, int Tn) {
 // as in the step (stream-K -> this kernel): 8 windows 14.3 -> 13.3 us, 32 windows 44.2 -> 43.7 us, 64 windows 91.6 ->
 // 78.1 us (the CTAs' dynamic scheduling leaves a smaller tail than the stream-K ranges' unit-boundary combines).
 // WT_CROSS_WINDOW=0 (a tuning knob) turns it off.
+int window_shape() {
+  static const int idx = [] {  // (read once; a function-local static initialises thread-safely)
+    const char *e = getenv("WT_CROSS_WIN_SHAPE");
+    const int v = e ? atoi(e) : 0;
+    return (v >= 0 && v < static_cast<int>(sizeof(kWinShapes) / sizeof(kWinShapes[0]))) ? v : 0;
+  }();
+  return idx;
+}
+
 bool window_kernel_ok(int W, int S, int H, int Tn) {
   static const int off = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_CROSS_WINDOW");
     return (e != nullptr && atoi(e) == 0) ? 1 : 0;
   }();
-  return !off && W > 0 && H > 0 && S <= 8 && cross_stream_slices_ok(Tn, kWinSlices);
+  return !off && W > 0 && H > 0 && S <= 8 && cross_stream_slices_ok(Tn, kWinShapes[window_shape()].slices);
+}
+
+template <typename T, int SL, int ST, int CT>
+int launch_window_shape(const CUtensorMap &km, const CUtensorMap &vm, const void *q, void *y, int *err, int W,
+                        int S, int H, int Tn, float scale, void *stream) {
+  constexpr int smem = win_smem(SL, ST);
+  const int st = opt_in_smem<cross_window_kernel<T, SL, ST, CT>>(smem, "cross_attn");
+  if (st != WT_OK) return st;
+  const int chunk = (Tn + SL - 1) / SL;
+  return launch("cross_attn", cross_window_kernel<T, SL, ST, CT>, dim3(W * H), dim3(SL * 32), smem, stream, km, vm,
+                static_cast<const T *>(q), static_cast<T *>(y), err, S, H, Tn, chunk, scale, wait_limit(),
+                test_withhold_stage());
+}
+
+template <typename T>
+int launch_window(const CUtensorMap &km, const CUtensorMap &vm, const void *q, void *y, int *err, int W, int S,
+                  int H, int Tn, float scale, void *stream) {
+  switch (window_shape()) {
+#define WT_WIN_CASE(i)                                                                                           \
+  case i:                                                                                                        \
+    return launch_window_shape<T, kWinShapes[i].slices, kWinShapes[i].stages, kWinShapes[i].ctas>(km, vm, q, y, err, \
+                                                                                                 W, S, H, Tn, scale, \
+                                                                                                 stream);
+    WT_WIN_CASE(1)
+#undef WT_WIN_CASE
+    default:
+      return launch_window_shape<T, kWinShapes[0].slices, kWinShapes[0].stages, kWinShapes[0].ctas>(km, vm, q, y, err,
+                                                                                                    W, S, H, Tn, scale,
+                                                                                                    stream);
+  }
 }
 
 // P = 0: the fused attention (a unit is a whole (window, head, query group)); P > 0: slice mode, P key slices of
@@ -864,21 +909,10 @@ int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y
     if (st != WT_OK) return st;
     st = encode_rows128_map(&vm, v, rows, 16, dtype);
     if (st != WT_OK) return st;
-    const int chunk = (Tn + kWinSlices - 1) / kWinSlices;
     const float scale = static_cast<float>(1.0 / 8.0 * 1.4426950408889634);
     int *err = static_cast<int *>(workspace);
-    if (dtype == WT_BF16) {
-      st = opt_in_smem<cross_window_kernel<__nv_bfloat16>>(kWinSmem, "cross_attn");
-      if (st != WT_OK) return st;
-      return launch("cross_attn", cross_window_kernel<__nv_bfloat16>, dim3(W * H), dim3(kWinSlices * 32), kWinSmem,
-                    stream, km, vm, static_cast<const __nv_bfloat16 *>(q), static_cast<__nv_bfloat16 *>(y), err, S,
-                    H, Tn, chunk, scale, wait_limit(), test_withhold_stage());
-    }
-    st = opt_in_smem<cross_window_kernel<__half>>(kWinSmem, "cross_attn");
-    if (st != WT_OK) return st;
-    return launch("cross_attn", cross_window_kernel<__half>, dim3(W * H), dim3(kWinSlices * 32), kWinSmem, stream,
-                  km, vm, static_cast<const __half *>(q), static_cast<__half *>(y), err, S, H, Tn, chunk, scale,
-                  wait_limit(), test_withhold_stage());
+    if (dtype == WT_BF16) return launch_window<__nv_bfloat16>(km, vm, q, y, err, W, S, H, Tn, scale, stream);
+    return launch_window<__half>(km, vm, q, y, err, W, S, H, Tn, scale, stream);
   }
   const int fp = P == 0 ? fused_slices(W, S, H, Tn) : 0;
   const StreamPlan p = fp > 0 ? plan_stream(W, S, H, Tn, fp, true) : plan_stream(W, S, H, Tn, P);
