@@ -327,9 +327,11 @@ def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) 
     mask_cur = torch.empty(1, W, dtype=torch.bool, device=dev)
     live_cur = torch.empty(1, W, dtype=torch.bool, device=dev)
 
-    def layer(i):
-        ap.self_attn_step_triton(qkv[i], cache[i, 0], cache[i, 1], offset, src, write_cache=True, out=y_self[i])
-        ap.cross_attn_triton(q[i], cross[i, 0], cross[i, 1], out=y_cross[i])
+    def layer(i, qkv_i=None, q_i=None):
+        """Layer i's attention (its qkv and cross queries, or the given copies of them)."""
+        ap.self_attn_step_triton(qkv[i] if qkv_i is None else qkv_i, cache[i, 0], cache[i, 1], offset, src,
+                                 write_cache=True, out=y_self[i])
+        ap.cross_attn_triton(q[i] if q_i is None else q_i, cross[i, 0], cross[i, 1], out=y_cross[i])
 
     def tail():
         """The step's bookkeeping from its schedule row (parent_cur .. rpos_cur): window replacements, then the
@@ -557,12 +559,14 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
     which the host writes into pinned staging before each step. The step's result is its last layer's attention
     outputs (self and cross), which the host reads back: the earlier layers' outputs feed the next layer on the
     device in a decoder and never cross PCIe (copying them all out too added 26 MB a step per rank, which 8 ranks
-    sharing the host's links could not move in a step's time). One CUDA graph per step: a copy-in stream brings the
-    layers' inputs in order, the compute stream runs layer i once its inputs have landed, so the PCIe transfers
-    overlap the HBM-bound kernels, and a copy-out stream takes the last layer's outputs back. Two steps are in
-    flight, as a serving loop keeps them: the host stages step s + 1's schedule row while step s runs (two pinned
-    staging and output buffers, one graph for each) and reads each step's result once that step's completion event
-    has fired, one step behind; nothing of a step's copies is skipped."""
+    sharing the host's links could not move in a step's time). One CUDA graph per step, the layers' inputs double-
+    buffered on the device: step s computes from buffer s % 2 while its copy stream brings step s + 1's inputs (52.4
+    MB at config 3) into the other buffer, so no layer waits for its own step's copy and a step costs the longer of
+    its kernels and its copy, not their sum; the step's schedule row goes in first on the same stream, and a copy-out
+    stream takes the last layer's outputs back after it. Two steps are in flight, as a serving loop keeps them: the
+    host stages step s + 1's schedule row while step s runs (two pinned staging and output buffers, one graph for
+    each) and reads each step's result once that step's completion event has fired, one step behind; every timed step
+    copies one step's inputs in and one result out."""
     W, K = sch.W, sch.K
     qkv_h = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
     q_h = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
@@ -582,8 +586,8 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
         st["rpos"].numpy().reshape(W)[:] = sch.refill_pos[s]
 
     n = qkv.shape[0]
+    qkv_buf, q_buf = (qkv, torch.empty_like(qkv)), (q, torch.empty_like(q))  # (buffer 0 holds step 0's inputs)
     cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(n)]
     ev_out = torch.cuda.Event()
     ev_sched = torch.cuda.Event()
 
@@ -592,16 +596,14 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
         cin.wait_stream(main)
         cout.wait_stream(main)
         with torch.cuda.stream(cin):
-            for i in range(n):
-                qkv[i].copy_(qkv_h[i], non_blocking=True)
-                q[i].copy_(q_h[i], non_blocking=True)
-                ev_in[i].record(cin)
             for k, v in cur.items():
                 v.copy_(stage[b][k], non_blocking=True)
             ev_sched.record(cin)
+            for i in range(n):  # the next step's inputs, under this step's kernels
+                qkv_buf[1 - b][i].copy_(qkv_h[i], non_blocking=True)
+                q_buf[1 - b][i].copy_(q_h[i], non_blocking=True)
         for i in range(n):
-            main.wait_event(ev_in[i])
-            layer(i)
+            layer(i, qkv_buf[b][i], q_buf[b][i])
         ev_out.record(main)
         cout.wait_event(ev_out)
         with torch.cuda.stream(cout):  # the step's result: the last layer's outputs
@@ -679,11 +681,11 @@ def run_e2e(torch, dev, layer, tail, qkv, q, y_self, y_cross, cur, steps, reset_
                         "note": "the layers' inputs copied alone from pinned host memory, every rank at once "
                                 "(slowest rank): the bound on the e2e step"},
             "path": "whisper_trt_b200.attn_plugin calls (C ABI) captured in a CUDA graph; every step the host "
-                    "stages the step's schedule row, the layers' qkv / queries and the schedule are copied in from "
-                    "pinned host memory (per layer, on a copy stream that overlaps the compute stream) and the "
-                    "step's result (the last layer's self and cross outputs) copied out; two steps in flight: the "
-                    "host stages step s + 1 while step s runs and reads each step's result when its completion "
-                    "event fires"}
+                    "stages the step's schedule row; the layers' qkv / queries are copied in from pinned host memory "
+                    "one step ahead, into the other of two device buffers on a copy stream under this step's "
+                    "kernels, and the step's result (the last layer's self and cross outputs) copied out; two steps "
+                    "in flight: the host stages step s + 1 while step s runs and reads each step's result when its "
+                    "completion event fires"}
 
 
 # --- the reference's CPU implementation ---------------------------------------------------------------------------
