@@ -285,6 +285,9 @@ def make_config(args, wl: dict, sch: Schedule, world: int) -> dict:
         cfg["bytes_per_step_logical"] = int(sum(sch.step_bytes(s, unique=False) for s in timed) / args.steps)
         cfg["bytes"] = ("unique: the shared prompt prefix counted once per window (its rows read it from the "
                         "window's first row); bytes_per_step_logical counts it per row")
+    if wl.get("prefilled"):
+        cfg["self_attn_prefix"] = ("per row" if args.no_shared_prefix else
+                                   f"once per window: self_attn_step_triton(shared_prefix_group={K})")
     return cfg
 
 
@@ -327,10 +330,13 @@ def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) 
     mask_cur = torch.empty(1, W, dtype=torch.bool, device=dev)
     live_cur = torch.empty(1, W, dtype=torch.bool, device=dev)
 
+    # a window's rows read one prefilled prompt through the slot table: its keys attended once per window
+    spg = K if (wl.get("prefilled") and not args.no_shared_prefix) else None
+
     def layer(i, qkv_i=None, q_i=None):
         """Layer i's attention (its qkv and cross queries, or the given copies of them)."""
         ap.self_attn_step_triton(qkv[i] if qkv_i is None else qkv_i, cache[i, 0], cache[i, 1], offset, src,
-                                 write_cache=True, out=y_self[i])
+                                 write_cache=True, out=y_self[i], shared_prefix_group=spg)
         ap.cross_attn_triton(q[i] if q_i is None else q_i, cross[i, 0], cross[i, 1], out=y_cross[i])
 
     def tail():
@@ -409,7 +415,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, light: bool = False) 
     for _ in range(args.warmup + args.steps // 2):
         graph.replay()
     torch.cuda.synchronize(dev)
-    ker = kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch)
+    ker = kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch, spg=spg)
 
     # end to end through the public API: H2D of the step's inputs from pinned memory, the step, D2H of its outputs
     e2e = None
@@ -486,7 +492,8 @@ def gpu_index(local_rank: int) -> int:
     return local_rank
 
 
-def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch, reps: int = 3) -> dict:
+def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, src, sch, reps: int = 3,
+                 spg=None) -> dict:
     """Device time per launch of each attention kernel, two ways (CUDA events on the launching stream, warm):
 
     * chained -- each kernel alone, its 32 layers' launches back to back in a CUDA graph (with programmatic dependent
@@ -523,7 +530,8 @@ def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, 
 
     def self_all():
         for i in range(L):
-            ap.self_attn_step_triton(qkv[i], cache[i, 0], cache[i, 1], offset, src, out=y_self[i])
+            ap.self_attn_step_triton(qkv[i], cache[i, 0], cache[i, 1], offset, src, out=y_self[i],
+                                     shared_prefix_group=spg)
 
     def cross_all():
         for i in range(L):
@@ -537,7 +545,8 @@ def kernel_times(torch, ap, dev, qkv, cache, cross, q, y_self, y_cross, offset, 
         for i in range(L):
             e = evs[r * L + i]
             e[0].record()
-            ap.self_attn_step_triton(qkv[i], cache[i, 0], cache[i, 1], offset, src, out=y_self[i])
+            ap.self_attn_step_triton(qkv[i], cache[i, 0], cache[i, 1], offset, src, out=y_self[i],
+                                     shared_prefix_group=spg)
             e[1].record()
             ap.cross_attn_triton(q[i], cross[i, 0], cross[i, 1], out=y_cross[i])
             e[2].record()
@@ -892,6 +901,8 @@ def main() -> None:
                      help="more workloads reported under 'also', at every N (comma-separated; '' = none)")
     ap_.add_argument("--no-ref-gpu", action="store_true",
                      help="skip the reference's Triton kernels timed beside these (N=1, rank 0)")
+    ap_.add_argument("--no-shared-prefix", action="store_true",
+                     help="config 4: attend each row's prompt prefix per row instead of once per window")
     ap_.add_argument("--no-pdl", action="store_true",
                      help="launch without programmatic dependent launch (default: with, WT_LAUNCH_PDL)")
     ap_.add_argument("--layers", type=int, default=32,
@@ -939,6 +950,8 @@ def main() -> None:
         if "bytes_per_step_logical" in a["config"]:
             res["also"][name]["bytes_per_step_logical"] = a["config"]["bytes_per_step_logical"]
             res["also"][name]["bytes"] = a["config"]["bytes"]
+        if "self_attn_prefix" in a["config"]:
+            res["also"][name]["self_attn_prefix"] = a["config"]["self_attn_prefix"]
     torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_ref_gpu:
         res["vs_reference_gpu"] = run_reference_gpu(local_rank)

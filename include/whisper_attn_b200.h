@@ -95,6 +95,22 @@ int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim);
 int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, const int64_t *offset,
                       const int32_t *src, void *y, int rows, int heads, int capacity, int head_dim,
                       int write_cache, int kv_splits, void *workspace, size_t workspace_bytes, void *stream);
+/* wt_self_attn_step_prefix: wt_self_attn_step (the same result, the same reference function, no key splits) for
+ *   rows that come in groups of `group` consecutive rows (1-8: a window's beams or samples) sharing a prefix of
+ *   their slot tables -- the prompt every row of a window reads from the window's first row, the beams' common
+ *   ancestry. Row a + n of the group starting at row a shares keys [0, p) with row a, p the first position below
+ *   min(offset[a + n], offset[a]) where their clamped slot-table entries differ (row a: its offset); when p >=
+ *   min_shared, a first kernel attends those keys once for the whole group (tensor cores, the group's queries as
+ *   one tile) and the step kernel after it attends the row's keys [p, offset) and the new token and merges the two.
+ *   Rows that share less than min_shared keys are attended as by wt_self_attn_step. Needs `workspace` of
+ *   wt_self_attn_step_prefix_workspace() bytes (no zeroing, any contents), not shared by calls that may overlap.
+ *   head_dim 64, capacity <= 1024. No counterpart in the reference (an added entry point; the grouping is the
+ *   caller's knowledge of its windows, which the reference's self_attn_step_triton does not receive). */
+size_t wt_self_attn_step_prefix_workspace(int rows, int heads, int head_dim);
+int wt_self_attn_step_prefix(int dtype, const void *qkv, void *k_cache, void *v_cache, const int64_t *offset,
+                             const int32_t *src, void *y, int rows, int heads, int capacity, int head_dim,
+                             int write_cache, int group, int min_shared, void *workspace, size_t workspace_bytes,
+                             void *stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Self-attention of S = new_tokens new tokens per row (a prompt) over the row's cache slots < offset[r] (each read

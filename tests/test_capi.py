@@ -64,6 +64,16 @@ def test_bad_arguments_return_status_without_a_gpu():
     assert st == _lib.WT_ERR_WORKSPACE
     st = lib.wt_cross_attn(0, p, p, p, p, 2, 5, 20, 1500, 64, None, 0, None)
     assert st == _lib.WT_ERR_WORKSPACE
+    pre = lambda dt, c, d, group, ms, ws, nb: lib.wt_self_attn_step_prefix(dt, p, p, p, p, p, p, 10, 20, c, d, 0,
+                                                                            group, ms, ws, nb, None)
+    assert pre(0, 96, 48, 5, 32, p, 1 << 20) == _lib.WT_ERR_UNSUPPORTED  # head_dim 64 only
+    assert pre(0, 96, 64, 0, 32, p, 1 << 20) == _lib.WT_ERR_ARG  # group 1-8
+    assert pre(0, 96, 64, 9, 32, p, 1 << 20) == _lib.WT_ERR_ARG
+    assert pre(0, 96, 64, 5, 0, p, 1 << 20) == _lib.WT_ERR_ARG  # min_shared >= 1
+    assert pre(0, 2000, 64, 5, 32, p, 1 << 20) == _lib.WT_ERR_UNSUPPORTED  # no key splits
+    assert pre(7, 96, 64, 5, 32, p, 1 << 20) == _lib.WT_ERR_DTYPE
+    assert pre(0, 96, 64, 5, 32, None, 0) == _lib.WT_ERR_WORKSPACE
+    assert pre(0, 96, 64, 5, 32, p, 100) == _lib.WT_ERR_WORKSPACE
     st = lib.wt_beam_scores(*([p] * 11), 2, 5, 51866, 16, 0, 50362, 0, 0, 50257, None, 0, None)
     assert st == _lib.WT_ERR_WORKSPACE
     st = lib.wt_beam_scores(*([p] * 11), 2, 9, 51866, 16, 0, 50362, 0, 0, 50257, p, 1 << 20, None)

@@ -112,7 +112,8 @@ template <typename T, int D, int LPK, int U, int kStages>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
     self_step_kernel(const T *__restrict__ qkv, T *kc, T *vc, const int64_t *__restrict__ offset,
                      const int32_t *__restrict__ src, T *__restrict__ y, float *__restrict__ part,
-                     int *__restrict__ counters, int N, int H, int C, int write_cache, int splits, float scale) {
+                     int *__restrict__ counters, int N, int H, int C, int write_cache, int splits, float scale,
+                     int group, int min_shared, const float *__restrict__ xrec) {
   constexpr int CPL = D / (8 * LPK);  // 16-byte pieces per lane of a key row
   constexpr int NA = 8 * CPL;         // head dims per lane
   constexpr int GPW = 32 / LPK;       // key groups per warp
@@ -137,18 +138,48 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   // (the whole slice, not only the slots below the offset: its loads then go out together with the offset's)
   const int64_t off64 = offset[r];
   const int32_t *srow = src + static_cast<size_t>(r) * C + lo;
+  // (shared-prefix mode, xrec given, no key splits) the keys [0, p) this row shares with its group's first row a --
+  // the first j below min(off, off_a) where the clamped slot tables differ, as the prefix pass finds it -- were
+  // attended by that pass (the kernel launched just before this one) when p >= min_shared: this CTA takes [p, off)
+  // and the new token and merges the pass's record at the end. Row a's entries are compared as the row's own are
+  // staged (the same round trip).
+  const int a = xrec != nullptr ? (r / group) * group : r;
+  const int64_t oa64 = xrec != nullptr ? offset[a] : 0;
+  const int32_t *sa = src + static_cast<size_t>(a) * C + lo;
+  int mism = C;
   for (int i = threadIdx.x; i < lim; i += kWarpsPerCta * 32) {
     const int v = srow[i];
-    rows_s[i] = v < 0 ? 0 : (v > N - 1 ? N - 1 : v);
+    const int cv = v < 0 ? 0 : (v > N - 1 ? N - 1 : v);
+    rows_s[i] = cv;
+    if (a != r) {
+      const int va = sa[i];
+      if ((va < 0 ? 0 : (va > N - 1 ? N - 1 : va)) != cv) mism = min(mism, i);
+    }
+  }
+  int *p_w = rows_s + (cap + 3) / 4 * 4;  // [warp]: the warps' first mismatches
+  if (xrec != nullptr) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mism = min(mism, __shfl_xor_sync(0xffffffffu, mism, o));
+    if (lane == 0) p_w[warp] = mism;
   }
   const int off = static_cast<int>(off64 < 0 ? 0 : (off64 > C ? C : off64));
-  const int hi = max(lo, min(off, lo + cap));  // keys [lo, hi) of this split
   __syncthreads();
+  int klo = lo;
+  bool shared = false;
+  if (xrec != nullptr) {
+    const int off_a = static_cast<int>(oa64 < 0 ? 0 : (oa64 > C ? C : oa64));
+    int p = min(off, off_a);
+#pragma unroll
+    for (int w2 = 0; w2 < kWarpsPerCta; ++w2) p = min(p, p_w[w2]);
+    shared = p >= min_shared;
+    if (shared) klo = p;
+  }
+  const int hi = max(klo, min(off, lo + cap));  // keys [klo, hi) of this split
 
   // this warp's quarter: whole stages [st0, st1) of the split's range
-  const int nst_all = (hi - lo + KPS - 1) / KPS;
+  const int nst_all = (hi - klo + KPS - 1) / KPS;
   const int st0 = nst_all * warp / kWarpsPerCta, st1 = nst_all * (warp + 1) / kWarpsPerCta;
-  const int wlo = lo + st0 * KPS, whi = min(hi, lo + st1 * KPS);
+  const int wlo = klo + st0 * KPS, whi = min(hi, klo + st1 * KPS);
   const int nst = st1 - st0;
   const size_t row_stride = static_cast<size_t>(H) * C * D;
   const T *kh = kc + static_cast<size_t>(h) * C * D + sub * 8;
@@ -315,6 +346,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32)
   }
   const int rh = r * H + h;
   T *yo = y + static_cast<size_t>(r) * HD + static_cast<size_t>(h) * D + sub * 8;
+  if (shared) {  // the prefix pass's state of keys [0, p) (the kernel launched before this one, complete)
+    const float *xr = xrec + static_cast<size_t>(rh) * (D + 2);
+    float acc2[NA];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc2[8 * c + k] = xr[(c * LPK + sub) * 8 + k];
+    merge_state(m, l, acc, xr[D], xr[D + 1], acc2);
+  }
   if (splits == 1) {
     const float inv = 1.f / l;
 #pragma unroll
@@ -378,9 +418,10 @@ size_t step_workspace(int rows, int heads, int head_dim, int splits) {
 
 template <typename T, int D, int LPK, int U, int kStages>
 int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y, int N,
-                int H, int C, int write_cache, int splits, void *ws, void *stream) {
+                int H, int C, int write_cache, int splits, void *ws, void *stream, int group, int min_shared,
+                const float *xrec) {
   const int cap = (C + splits - 1) / splits;
-  const int smem = kWarpsPerCta * ring_bytes<U, D / (8 * LPK), kStages>() + (cap * 4 + 15) / 16 * 16;
+  const int smem = kWarpsPerCta * ring_bytes<U, D / (8 * LPK), kStages>() + (cap * 4 + 15) / 16 * 16 + 16;
   auto kernel = self_step_kernel<T, D, LPK, U, kStages>;
   const int st = opt_in_smem<self_step_kernel<T, D, LPK, U, kStages>>(smem, "self_attn_step");
   if (st != WT_OK) return st;
@@ -394,7 +435,7 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(D)) * 1.4426950408889634);
   return launch("self_attn_step", kernel, dim3(N * H, splits), dim3(kWarpsPerCta * 32), smem, stream,
                 static_cast<const T *>(qkv), static_cast<T *>(kc), static_cast<T *>(vc), offset, src,
-                static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale);
+                static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale, group, min_shared, xrec);
 }
 
 // Shape (lanes per key row, keys per lane group per stage, stages) of the head_dim 64 kernel. By default it follows
@@ -417,9 +458,11 @@ int self_shape(int cap) {
 
 template <typename T>
 int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *offset, const int32_t *src, void *y,
-                  int N, int H, int C, int write_cache, int splits, void *ws, void *stream) {
-#define WT_STEP(D_, LPK_, U_, S_) \
-  launch_step<T, D_, LPK_, U_, S_>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream)
+                  int N, int H, int C, int write_cache, int splits, void *ws, void *stream, int group = 0,
+                  int min_shared = 0, const float *xrec = nullptr) {
+#define WT_STEP(D_, LPK_, U_, S_)                                                                          \
+  launch_step<T, D_, LPK_, U_, S_>(qkv, kc, vc, offset, src, y, N, H, C, write_cache, splits, ws, stream, group, \
+                                   min_shared, xrec)
   switch (D) {
     case 16: return WT_STEP(16, 2, 4, 2);
     case 32: return WT_STEP(32, 4, 4, 2);
@@ -438,6 +481,10 @@ int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *off
 }
 
 }  // namespace
+
+int self_prefix_pass(int dtype, const void *qkv, const void *kc, const void *vc, const int64_t *offset,
+                     const int32_t *src, float *rec, int N, int H, int C, int group, int min_shared, void *stream);
+
 }  // namespace wt
 
 extern "C" {
@@ -460,6 +507,54 @@ int wt_self_attn_step_splits(int rows, int heads, int capacity, int head_dim) {
 size_t wt_self_attn_step_workspace(int rows, int heads, int head_dim, int kv_splits) {
   if (rows <= 0 || heads <= 0 || head_dim <= 0) return 0;
   return wt::step_workspace(rows, heads, head_dim, kv_splits);
+}
+
+size_t wt_self_attn_step_prefix_workspace(int rows, int heads, int head_dim) {
+  if (rows <= 0 || heads <= 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(rows) * heads * (head_dim + 2) * sizeof(float);
+}
+
+int wt_self_attn_step_prefix(int dtype, const void *qkv, void *k_cache, void *v_cache, const int64_t *offset,
+                             const int32_t *src, void *y, int rows, int heads, int capacity, int head_dim,
+                             int write_cache, int group, int min_shared, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+  using namespace wt;
+  WT_REQUIRE(rows > 0 && heads > 0 && capacity > 0 && head_dim > 0, WT_ERR_ARG,
+             "self_attn_step_prefix: sizes must be positive (rows %d, heads %d, capacity %d, head_dim %d)", rows,
+             heads, capacity, head_dim);
+  WT_REQUIRE(qkv && k_cache && v_cache && offset && src && y, WT_ERR_ARG, "self_attn_step_prefix: null pointer");
+  WT_ALIGNED(qkv);
+  WT_ALIGNED(k_cache);
+  WT_ALIGNED(v_cache);
+  WT_ALIGNED(offset);
+  WT_ALIGNED(src);
+  WT_ALIGNED(y);
+  WT_REQUIRE(head_dim == 64, WT_ERR_UNSUPPORTED, "self_attn_step_prefix: head_dim %d (this build: 64)", head_dim);
+  WT_REQUIRE(group >= 1 && group <= 8, WT_ERR_ARG, "self_attn_step_prefix: group %d (1-8 rows)", group);
+  WT_REQUIRE(min_shared >= 1, WT_ERR_ARG, "self_attn_step_prefix: min_shared %d must be positive", min_shared);
+  WT_REQUIRE(capacity <= kMaxSplitKeys, WT_ERR_UNSUPPORTED,
+             "self_attn_step_prefix: capacity %d > %d (use wt_self_attn_step with key splits)", capacity,
+             kMaxSplitKeys);
+  WT_REQUIRE(static_cast<long long>(rows) * heads < (1LL << 31), WT_ERR_ARG,
+             "self_attn_step_prefix: rows*heads too large");
+  WT_REQUIRE(dtype == WT_F16 || dtype == WT_BF16, WT_ERR_DTYPE, "self_attn_step_prefix: unknown dtype %d", dtype);
+  const size_t need = wt_self_attn_step_prefix_workspace(rows, heads, head_dim);
+  WT_REQUIRE(workspace && workspace_bytes >= need, WT_ERR_WORKSPACE,
+             "self_attn_step_prefix: needs a workspace of %zu bytes (given %zu)", need,
+             workspace ? workspace_bytes : 0);
+  WT_ALIGNED(workspace);
+  float *rec = static_cast<float *>(workspace);
+  // the prefix pass first (the shared rows' prefixes into the workspace), then the step kernel (every row's keys
+  // past its shared prefix, the new token and the append, merged with the pass's record). (The other order -- the
+  // step kernel's states merged by the pass -- measured slower: config 4's step 1.395 against 1.335 ms.)
+  int st = self_prefix_pass(dtype, qkv, k_cache, v_cache, offset, src, rec, rows, heads, capacity, group, min_shared,
+                            stream);
+  if (st != WT_OK) return st;
+  if (dtype == WT_F16)
+    return dispatch_step<__half>(head_dim, qkv, k_cache, v_cache, offset, src, y, rows, heads, capacity, write_cache,
+                                 1, nullptr, stream, group, min_shared, rec);
+  return dispatch_step<__nv_bfloat16>(head_dim, qkv, k_cache, v_cache, offset, src, y, rows, heads, capacity,
+                                      write_cache, 1, nullptr, stream, group, min_shared, rec);
 }
 
 int wt_self_attn_step(int dtype, const void *qkv, void *k_cache, void *v_cache, const int64_t *offset,

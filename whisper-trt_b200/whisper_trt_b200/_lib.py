@@ -27,6 +27,9 @@ SIGNATURES = {
     "wt_self_attn_step_splits": (c_int, [c_int, c_int, c_int, c_int]),
     "wt_self_attn_step": (c_int, [c_int, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int,
                                   c_int, c_int, c_void, c_size, c_void]),
+    "wt_self_attn_step_prefix_workspace": (c_size, [c_int, c_int, c_int]),
+    "wt_self_attn_step_prefix": (c_int, [c_int, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int,
+                                         c_int, c_int, c_int, c_int, c_void, c_size, c_void]),
     "wt_self_attn": (c_int, [c_int, c_void, c_void, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int,
                              c_void]),
     "wt_cross_attn_split": (c_int, [c_int, c_void, c_void, c_void, c_void, c_int, c_int, c_int, c_int, c_int, c_int,

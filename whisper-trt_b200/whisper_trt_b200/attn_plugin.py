@@ -18,6 +18,7 @@ run each shape once before capturing it, as the reference's own capture does (se
 
 from __future__ import annotations
 
+import functools
 import math
 
 import torch
@@ -102,13 +103,17 @@ def self_attn_step_config(rows: int, heads: int = 20, capacity: int = 448, head_
 
 def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: torch.Tensor,
                           src: torch.Tensor, config=None, write_cache: bool = False, *, kv_splits: int | None = None,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
+                          out: torch.Tensor | None = None, shared_prefix_group: int | None = None,
+                          min_shared: int = 32) -> torch.Tensor:
     """Self-attention of one new token per row (qkv [N, 1, 3*H*D]) over its cache slots < offset, read through
     ``src``, and the new token -> [N, 1, H*D] in qkv's dtype. ``write_cache``: the new keys/values also go into the
     caches at ``offset`` (in place). Reference: attn_plugin.py:488-501 (kernel :309-350).
 
     ``config`` is accepted for call-compatibility and ignored; ``kv_splits`` (None: chosen from the shape) splits
-    every row's cache into that many parts (at least ceil(C / 1024))."""
+    every row's cache into that many parts (at least ceil(C / 1024)). ``shared_prefix_group`` (an addition: the
+    rows per window, 1-8): the rows of each group of that many consecutive rows that share at least ``min_shared``
+    leading slot-table entries with the group's first row have those keys attended once for the whole group
+    (``wt_self_attn_step_prefix``); the result is the same attention. Head dim 64, C <= 1024, no key splits."""
     what = "self_attn_step"
     if qkv.dim() != 3:
         raise ValueError(f"{what}: qkv must be [N, S, 3*H*D]")
@@ -132,6 +137,18 @@ def self_attn_step_triton(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     if y.shape != (n, 1, h * d) or y.dtype != qkv.dtype:
         raise ValueError(f"{what}: out must be [N, 1, H*D] of qkv's dtype")
     lib = _lib.load()
+    if shared_prefix_group:
+        if kv_splits not in (None, 1):
+            raise ValueError(f"{what}: shared_prefix_group takes no key splits")
+        ws_bytes = int(lib.wt_self_attn_step_prefix_workspace(n, h, d))
+        ws = _workspace(dev, "self_prefix", (n, h, d), ws_bytes)
+        with torch.cuda.device(dev):
+            st = lib.wt_self_attn_step_prefix(code, qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                              offset.data_ptr(), src.data_ptr(), y.data_ptr(), n, h, c, d,
+                                              int(bool(write_cache)), int(shared_prefix_group), int(min_shared),
+                                              ws.data_ptr(), ws_bytes, _stream(dev))
+        _lib.check(st, what)
+        return y
     splits = int(kv_splits) if kv_splits else int(lib.wt_self_attn_step_splits(n, h, c, d))
     splits = max(splits, -(-c // 1024))  # (at most 1024 cache slots per split)
     ws_ptr, ws_bytes = None, 0
@@ -405,9 +422,13 @@ def _(part, q):
     return torch.empty_like(q)
 
 
-def install(module) -> None:
+def install(module, shared_prefix_group: int | None = None) -> None:
     """Route a reference ``whisper_trt.attn_plugin`` module's launchers to these kernels (in place), so its callers
-    -- ``TritonDecoderBackend.step_fn`` (runtime.py:134-151) among them -- run on them unchanged."""
+    -- ``TritonDecoderBackend.step_fn`` (runtime.py:134-151) among them -- run on them unchanged.
+    ``shared_prefix_group`` (the caller's rows per window, e.g. its beam or sample count): the decode-step
+    self-attention then attends the keys a window's rows share through the slot table once per window."""
     for name in ("self_attn_triton", "self_attn_step_triton", "cross_attn_split_triton",
                  "cross_attn_combine_triton", "cross_attn_triton", "self_attn_step_config", "logits32_triton"):
         setattr(module, name, globals()[name])
+    if shared_prefix_group:
+        module.self_attn_step_triton = functools.partial(self_attn_step_triton, shared_prefix_group=shared_prefix_group)
