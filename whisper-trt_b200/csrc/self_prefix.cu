@@ -111,6 +111,9 @@ __global__ void __launch_bounds__(kPxWarps * 32)
   auto clamp_row = [N](int v) { return v < 0 ? 0 : (v > N - 1 ? N - 1 : v); };
   auto clamp_off = [C](int64_t v) { return static_cast<int>(v < 0 ? 0 : (v > C ? C : v)); };
   const int off_a = clamp_off(offset[a]);
+  // every member's shared prefix lies in the first row's keys [0, off_a), which the first row itself shares whole:
+  // nothing to do below min_shared (uniform over the CTA), else those keys are the ones to gather
+  if (off_a < min_shared) return;
   if (threadIdx.x < kPxMaxGroup) plen[threadIdx.x] = threadIdx.x < ng ? min(clamp_off(offset[a + threadIdx.x]), off_a) : 0;
   const int32_t *sa = src + static_cast<size_t>(a) * C;
   // the members' entries in 4-entry chunks, (member, chunk) pairs spread over the threads, four loads in flight per
@@ -133,6 +136,34 @@ __global__ void __launch_bounds__(kPxWarps * 32)
   load4(threadIdx.x);
   for (int j = threadIdx.x; j < C; j += kStride) src_a[j] = clamp_row(sa[j]);
   __syncthreads();
+  // this warp's 16-key blocks [b0, b1) of the prefix; the first stages' copies go out now, the members' scan (which
+  // sets each query's key range, not the keys) runs while they are in flight
+  const int pmax = off_a;
+  const int nblk = (pmax + 15) / 16;
+  const int b0 = nblk * warp / kPxWarps, b1 = nblk * (warp + 1) / kPxWarps;
+  const int nw = b1 - b0;
+  const size_t row_stride = static_cast<size_t>(H) * C * kD;
+  const T *kh = kc + static_cast<size_t>(h) * C * kD;
+  const T *vh = vc + static_cast<size_t>(h) * C * kD;
+  // block b into stage s: lane covers rows lane / 8 + 4 i (i < 4), 16-byte chunk lane % 8 of each, swizzled
+  auto issue = [&](int b, int s) {
+    unsigned char *kt = ring + s * kPxStage, *vt = kt + kPxTile;
+    const int ch = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = (lane >> 3) + 4 * i, j = b * 16 + rr;
+      const bool ok = j < pmax;
+      const size_t o = ok ? static_cast<size_t>(src_a[j]) * row_stride + static_cast<size_t>(j) * kD + ch * 8 : 0;
+      cp_async16_zfill(kt + swizzle128(rr, ch), kh + o, ok);
+      cp_async16_zfill(vt + swizzle128(rr, ch), vh + o, ok);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < kPxStages - 1; ++s) {
+    if (s < nw) issue(b0 + s, s);
+    px_commit();
+  }
+
   if (vec) {
     for (int i0 = threadIdx.x; i0 < total; i0 += 4 * kStride) {
       if (i0 != static_cast<int>(threadIdx.x)) load4(i0);
@@ -161,39 +192,8 @@ __global__ void __launch_bounds__(kPxWarps * 32)
   }
   __syncthreads();
   // a query column takes part when its row is shared: keys [0, lim) of column n
-  int pmax = 0;
-#pragma unroll
-  for (int n = 0; n < kPxMaxGroup; ++n)
-    if (n < ng && plen[n] >= min_shared) pmax = max(pmax, plen[n]);
   const int nb = (2 * c < ng && plen[2 * c] >= min_shared) ? plen[2 * c] : 0;
   const int nb1 = (2 * c + 1 < ng && plen[2 * c + 1] >= min_shared) ? plen[2 * c + 1] : 0;
-  if (pmax == 0) return;  // (no shared row in this group: uniform over the CTA)
-
-  // this warp's 16-key blocks [b0, b1) of the prefix
-  const int nblk = (pmax + 15) / 16;
-  const int b0 = nblk * warp / kPxWarps, b1 = nblk * (warp + 1) / kPxWarps;
-  const int nw = b1 - b0;
-  const size_t row_stride = static_cast<size_t>(H) * C * kD;
-  const T *kh = kc + static_cast<size_t>(h) * C * kD;
-  const T *vh = vc + static_cast<size_t>(h) * C * kD;
-  // block b into stage s: lane covers rows lane / 8 + 4 i (i < 4), 16-byte chunk lane % 8 of each, swizzled
-  auto issue = [&](int b, int s) {
-    unsigned char *kt = ring + s * kPxStage, *vt = kt + kPxTile;
-    const int ch = lane & 7;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = (lane >> 3) + 4 * i, j = b * 16 + rr;
-      const bool ok = j < pmax;
-      const size_t o = ok ? static_cast<size_t>(src_a[j]) * row_stride + static_cast<size_t>(j) * kD + ch * 8 : 0;
-      cp_async16_zfill(kt + swizzle128(rr, ch), kh + o, ok);
-      cp_async16_zfill(vt + swizzle128(rr, ch), vh + o, ok);
-    }
-  };
-#pragma unroll
-  for (int s = 0; s < kPxStages - 1; ++s) {
-    if (s < nw) issue(b0 + s, s);
-    px_commit();
-  }
 
   pdl_wait();
   pdl_launch_dependents();
