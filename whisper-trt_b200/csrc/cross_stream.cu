@@ -67,7 +67,6 @@ struct StreamArgs {
   int *err;
   float *slices_out;  // slice mode: the reference's partials [W, H, P, S, D + 2] instead of y (null: fused output)
   int P, chunk;       // key slices per (window, head) and keys per slice (fused: 1 and Tn)
-  int fuse_slices;    // fused output from slice units: each slice's partial to the workspace, the last one combines
   int W, S, H, Tn, QG, bpu;
   long long total;
   long long per_warp;
@@ -179,21 +178,6 @@ template <typename T, int NT>
 __device__ __forceinline__ void finalize_unit(State<NT> &st, const StreamArgs &a, long long u, int lane) {
   const int g = lane >> 2, c = lane & 3;
   const UnitPos p = unit_pos(a, u);
-  if (a.fuse_slices) {  // this slice's record, counted; the (window, head, query group)'s last slice combines
-    const long long grp = (static_cast<long long>(p.w) * a.H + p.h) * a.QG + p.qg;
-    const float *base = a.part + static_cast<size_t>(grp) * a.P * (NT * 8) * kPart;
-    write_record<NT>(st, a.part + (static_cast<size_t>(grp) * a.P + p.sl) * (NT * 8) * kPart, lane);
-    __syncwarp();
-    int old = 0;
-    if (lane == 0)
-      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + grp) : "memory");
-    if (__shfl_sync(0xffffffffu, old + 1 == a.P ? 1 : 0, 0)) {
-      __syncwarp();
-      combine_records<T, NT>(a, base, a.P, p, lane);
-      if (lane == 0) a.counters[grp] = 0;  // left zeroed for the next launch
-    }
-    return;
-  }
   const int w = p.w, h = p.h, qg = p.qg;
   const size_t HD = static_cast<size_t>(a.H) * kD;
   T *y = static_cast<T *>(a.y);
@@ -727,27 +711,10 @@ int forced_shape() {
 }
 
 struct StreamPlan {
-  int nt, qgs, bpu, max_slots, grid, shape, slices, chunk, fuse;
+  int nt, qgs, bpu, max_slots, grid, shape, slices, chunk;
   long long units, total, per_warp;
   size_t counters_off, part_off, bytes;
 };
-
-// Fused attention of few windows: slice units of ~12 blocks (one wave of warps at most) whose partials the last slice of
-// each (window, head) combines, instead of the persistent stream-K ranges (measured at 8 windows: 12.4 us per launch for
-// the slice units against 15.0). WT_CROSS_FUSE (a tuning knob) forces it on (1) or off (0).
-int fused_slices(int W, int S, int H, int Tn) {
-  static const int forced = [] {  // (read once; a function-local static initialises thread-safely)
-    const char *e = getenv("WT_CROSS_FUSE");
-    return e ? (atoi(e) != 0 ? 1 : 0) : -1;
-  }();
-  if (forced == 0 || S > 8) return 0;
-  const int bpu = (Tn + 15) / 16;
-  const int P = (bpu + 11) / 12;
-  if (P < 2 || !cross_stream_slices_ok(Tn, P)) return 0;
-  const long long resident = static_cast<long long>(sm_count()) * kShapes[2].ctas * kShapes[2].warps;
-  if (forced == 1 || static_cast<long long>(W) * H * P <= resident) return P;
-  return 0;
-}
 
 // The one-CTA-per-(window, head) kernel takes the fused attention when a window has at most 8 queries (one query
 // tile) and every 16-key block of the 8 slices holds a key; the stream-K kernel the rest. Measured per launch, chained
@@ -802,11 +769,9 @@ int launch_window(const CUtensorMap &km, const CUtensorMap &vm, const void *q, v
 }
 
 // P = 0: the fused attention (a unit is a whole (window, head, query group)); P > 0: slice mode, P key slices of
-// ceil(Tn / P) keys per (window, head), each its own unit -- with `fuse`, the slices' partials are combined into the
-// output in-kernel instead of written as the reference's part.
-StreamPlan plan_stream(int W, int S, int H, int Tn, int P, bool fuse = false) {
+// ceil(Tn / P) keys per (window, head), each its own unit, written as the reference's part.
+StreamPlan plan_stream(int W, int S, int H, int Tn, int P) {
   StreamPlan p{};
-  p.fuse = fuse ? 1 : 0;
   p.nt = (S + 7) / 8 > 4 ? 4 : (S + 7) / 8;
   p.qgs = (S + p.nt * 8 - 1) / (p.nt * 8);
   p.slices = P > 0 ? P : 1;
@@ -840,9 +805,8 @@ StreamPlan plan_stream(int W, int S, int H, int Tn, int P, bool fuse = false) {
   p.max_slots = static_cast<int>((p.bpu + p.per_warp - 1) / p.per_warp + 1);
   p.counters_off = 256;  // [0, 256): the device error word
   p.part_off = p.counters_off + (static_cast<size_t>(p.units) * sizeof(int) + 255) / 256 * 256;
-  // (slice mode shares no unit between warps: no partials; fused from slices, one record per slice)
-  p.bytes = p.part_off + (P > 0 ? (fuse ? static_cast<size_t>(p.units) * p.nt * 8 * kPart * sizeof(float) : 0)
-                                : static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float));
+  // (slice mode shares no unit between warps: no partials)
+  p.bytes = p.part_off + (P > 0 ? 0 : static_cast<size_t>(p.units) * p.max_slots * p.nt * 8 * kPart * sizeof(float));
   return p;
 }
 
@@ -883,10 +847,6 @@ int launch_stream_nt(const CUtensorMap &km, const CUtensorMap &vm, const StreamA
 
 size_t cross_stream_workspace(int W, int S, int H, int Tn, int P) {
   if (P == 0 && window_kernel_ok(W, S, H, Tn)) return 256;  // (the device error word only)
-  if (P == 0) {
-    const int fp = fused_slices(W, S, H, Tn);
-    if (fp > 0) return plan_stream(W, S, H, Tn, fp, true).bytes;
-  }
   return plan_stream(W, S, H, Tn, P).bytes;
 }
 
@@ -914,8 +874,7 @@ int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y
     if (dtype == WT_BF16) return launch_window<__nv_bfloat16>(km, vm, q, y, err, W, S, H, Tn, scale, stream);
     return launch_window<__half>(km, vm, q, y, err, W, S, H, Tn, scale, stream);
   }
-  const int fp = P == 0 ? fused_slices(W, S, H, Tn) : 0;
-  const StreamPlan p = fp > 0 ? plan_stream(W, S, H, Tn, fp, true) : plan_stream(W, S, H, Tn, P);
+  const StreamPlan p = plan_stream(W, S, H, Tn, P);
   WT_REQUIRE(workspace && workspace_bytes >= p.bytes, WT_ERR_WORKSPACE,
              "cross_attn: needs a zeroed workspace of %zu bytes (given %zu)", p.bytes, workspace ? workspace_bytes : 0);
   WT_REQUIRE(p.total < (1LL << 40), WT_ERR_ARG, "cross_attn: too large");
@@ -927,7 +886,7 @@ int cross_stream(int dtype, const void *q, const void *k, const void *v, void *y
   if (st != WT_OK) return st;
   char *ws = static_cast<char *>(workspace);
   StreamArgs a{q,       y,    reinterpret_cast<float *>(ws + p.part_off), reinterpret_cast<int *>(ws + p.counters_off),
-               reinterpret_cast<int *>(ws), P > 0 ? slices_out : nullptr, p.slices, p.chunk, p.fuse, W, S, H, Tn, p.qgs,
+               reinterpret_cast<int *>(ws), P > 0 ? slices_out : nullptr, p.slices, p.chunk, W, S, H, Tn, p.qgs,
                p.bpu, p.total, p.per_warp, p.max_slots,
                static_cast<float>(1.0 / 8.0 * 1.4426950408889634), wait_limit(), test_withhold_stage()};
   const bool bf = dtype == WT_BF16;
