@@ -268,20 +268,6 @@ __device__ __forceinline__ void smem_frags(uint32_t (&ka)[4][4], uint32_t (&va)[
   for (int i = 0; i < 4; ++i) ldmatrix_x4_trans(va[i], vt + swizzle128(vrow, 2 * i + vchunk_hi));
 }
 
-// A real instruction that reads the given fragment registers: after it, the warp-wide ldmatrix loads that produced
-// them have completed (their shared-memory reads are done), so the tile they came from may be overwritten.
-__device__ __forceinline__ void consume_frags(const uint32_t (&ka)[4][4], const uint32_t (&va)[4][4]) {
-  asm volatile(
-      "{\n"
-      ".reg .b32 t;\n"
-      "xor.b32 t, %0, %1;\n"
-      "xor.b32 t, t, %2;\n"
-      "xor.b32 t, t, %3;\n"
-      "}\n" ::"r"(ka[3][3]),
-      "r"(va[3][3]), "r"(ka[0][0]), "r"(va[0][0])
-      : "memory");
-}
-
 // Query B fragments in the standard layout: lane (g, c) holds query g's head-dim pairs (16s+2c, +1) and
 // (16s+2c+8, +9), i.e. 32-bit words c + 4j (j = 0..7) of the query row.
 template <typename T, int NT>

@@ -22,7 +22,8 @@
 //     unit's count, due in mid-range, is left to the CTA's one service warp, which issues no loads: the streaming
 //     warp stores its partial and arrives on an mbarrier (a CTA-scope release), and the service warp fences and
 //     counts. The last unit is counted by its warp at the end of its range, when nothing of its own is in flight.
-// Every mbarrier wait is bounded: a wait that times out records an error code in the workspace and the warp goes on.
+// Every mbarrier wait is bounded: a wait that times out records an error code in the workspace, and the warp stops
+// streaming, waits (bounded) for the copies it still has in flight and leaves its units unfinished.
 // With programmatic dependent launch the first TMA loads are issued before the preceding kernel has finished (the
 // cross keys/values are not its output); the queries are read after it, one unit ahead of their use.
 #include <cstdlib>
@@ -40,6 +41,17 @@ constexpr int kTileBytes = 16 * 128;         // 16 keys x 64 elements x 2 bytes
 constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
 constexpr int kErrTimeout = 1;
 constexpr int kPart = kD + 4;  // floats per query of a partial: acc[64], m, l, 2 pad (16-byte aligned records)
+
+// A warp hands stages it has read back to the TMA: every lane's shared-memory reads of them (ldmatrix, generic proxy)
+// are ordered before the copies that refill them (async proxy) by a proxy fence in each lane, then a warp barrier,
+// after which one lane issues the copies. Without the fence nothing orders the two proxies: the compiler may sink a
+// fragment load below the copy's issue, and the copy then overwrites the tile before the load reads it (measured at
+// 16 queries per window, 20 heads x 1500 frames: without the fence most launches had one (window, head) wrong, with
+// it none of 40).
+__device__ __forceinline__ void release_stages() {
+  fence_proxy_async_smem();
+  __syncwarp();
+}
 
 // Launch shapes: streaming warps per CTA (plus the service warp) x ring stages per warp x CTAs per SM. Shared
 // memory: warps * stages * 4 KB per CTA. Small problems (under 24 blocks per warp with shape 2) take shape 2,
@@ -431,7 +443,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   State<NT> st;
   long long cur = -1;
   int nblk = 0;
-  uint32_t late = 0;  // stages whose wait timed out (their copies may still be in flight)
+  int stop = -1;  // the block whose wait timed out: nothing is consumed or issued from it on
   // Only a range's first unit (when it began in an earlier warp's range) and its last one (when it goes on into the
   // next warp's range) are shared with other warps: they go through partials and the units' counters; a unit wholly
   // inside the range goes straight to the output from registers. The first unit, when the range goes on past it, is
@@ -439,7 +451,8 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   // the GPU-scope fence a count needs, which would stall this warp -- with its loads in flight -- for about as long
   // as eight blocks take to stream (measured). The last unit is counted by this warp at the end of its range.
   const bool first_shared = beg % a.bpu != 0;
-  if (!(n > 0 && first_shared && beg + n > (u0 + 1) * a.bpu) && lane == 0) {  // no such unit: say so
+  bool handed = !(n > 0 && first_shared && beg + n > (u0 + 1) * a.bpu);  // the service warp's request is posted
+  if (handed && lane == 0) {  // no such unit: say so
     req_u[warp] = -1;
     mbar_arrive(&req_bar[warp]);
   }
@@ -458,6 +471,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
             req_n[warp] = nblk;
             mbar_arrive(&req_bar[warp]);
           }
+          handed = true;
         } else {
           finalize_unit<T, NT>(st, a, cur, lane);
         }
@@ -487,33 +501,35 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
     }
     // two blocks at once when the range's next block belongs to the same (window, head)
     const bool pair = kPair && j + 1 < n && c_b + 1 < a.bpu;
-    const int s0 = j % kStreamStages;
-    if (!mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kStreamStages) & 1), a.err, kErrTimeout, a.polls))
-      late |= 1u << s0;
+    const int s0 = j % kStreamStages, s1 = (j + 1) % kStreamStages;
+    // a wait that runs out (in any lane: the warp decides together) stops the range here, error word set: the stage
+    // is neither read nor refilled, so every stage keeps at most one copy outstanding and the drain below can wait
+    // for each by its own phase
+    bool ok = mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kStreamStages) & 1), a.err, kErrTimeout, a.polls);
+    if (pair && ok)
+      ok = mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kStreamStages) & 1), a.err, kErrTimeout,
+                             a.polls);
+    if (!__all_sync(0xffffffffu, ok)) {
+      stop = j;
+      break;
+    }
     uint32_t ka[4][4], va[4][4];
     smem_frags(ka, va, ring + s0 * kStageBytes, ring + s0 * kStageBytes + kTileBytes, lane);
     const int k0 = c_b * 16;
     const int klen = min(a.Tn - c_sl * a.chunk, a.chunk);  // keys of the unit's slice (fused: all Tn)
     const int used = pair ? 2 : 1;
     if (pair) {
-      const int s1 = (j + 1) % kStreamStages;
-      if (!mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kStreamStages) & 1), a.err, kErrTimeout,
-                             a.polls))
-        late |= 1u << s1;
       uint32_t kb[4][4], vb[4][4];
       smem_frags(kb, vb, ring + s1 * kStageBytes, ring + s1 * kStageBytes + kTileBytes, lane);
-      // the stages' operands are in registers (their shared-memory reads are complete): refill the stages now,
-      // so every stage of the ring is in flight while this warp computes
-      consume_frags(ka, va);
-      consume_frags(kb, vb);
-      __syncwarp();
+      // refill both stages now, so every stage of the ring is in flight while this warp computes: each lane's
+      // reads of them ordered before the copies (release_stages), then one lane issues
+      release_stages();
       if (lane == 0)
         for (int u = 0; u < used && issued < n; ++u) issue_next();
       const bool ok[2][2] = {{k0 + g < klen, k0 + g + 8 < klen}, {k0 + 16 + g < klen, k0 + 24 + g < klen}};
       attend_block2<T, NT>(st, ka, va, kb, vb, qf, ok, a.scale);
     } else {
-      consume_frags(ka, va);
-      __syncwarp();
+      release_stages();
       if (lane == 0 && issued < n) issue_next();
       attend_block<T, NT>(st, ka, va, qf, k0 + g < klen, k0 + g + 8 < klen, a.scale);
     }
@@ -532,6 +548,21 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
       }
     }
   }
+  if (stop >= 0) {
+    // a timed-out wait: before the shared memory goes away, wait (bounded, again) for every copy still outstanding
+    // -- blocks stop .. issued - 1, at most one per stage -- and leave the range's units unfinished (the output is
+    // invalid and the error word says so; the workspace must be zeroed again before its next use)
+    const int iss = __shfl_sync(0xffffffffu, issued, 0);
+    for (int jj = stop; jj < iss; ++jj)
+      if (!(withhold && jj == 0))
+        mbar_wait_bounded(&bars[jj % kStreamStages], static_cast<uint32_t>((jj / kStreamStages) & 1), nullptr, 0,
+                          a.polls);
+    if (!handed && lane == 0) {  // (the service warp is told there is nothing to count)
+      req_u[warp] = -1;
+      mbar_arrive(&req_bar[warp]);
+    }
+    return;
+  }
   // the last unit: shared if it began before the range or goes on after it (the loop did not step past its last block)
   const bool last_shared = cur >= 0 && ((cur == u0 && first_shared) || c_u == cur);
   if (cur >= 0) {
@@ -542,12 +573,6 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
   }
   if (last_shared) {
     if (__shfl_sync(0xffffffffu, publish(a, cur, nblk, lane) ? 1 : 0, 0)) combine_unit<T, NT>(a, cur, lane);
-  }
-  // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
-  for (int j = n - min(n, kStreamStages); j < n; ++j) {
-    const int s = j % kStreamStages;
-    if (late & (1u << s))
-      mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kStreamStages) & 1), nullptr, 0, a.polls);
   }
 }
 
@@ -614,25 +639,27 @@ __global__ void __launch_bounds__(kWinSlices * 32, kWinCtas)
   load_q_std<T, 1>(qf, q + static_cast<size_t>(w) * S * HD + static_cast<size_t>(h) * kD, HD, 0, S, g, c);
   State<1> st;
   reset_state<1>(st);
-  uint32_t late = 0;  // stages whose wait timed out (their copies may still be in flight)
+  int stop = -1;  // the block whose wait timed out: nothing is consumed or issued from it on
   for (int j = 0; j < nblk;) {
     const bool pair = j + 1 < nblk;
-    const int s0 = j % kWinStages;
-    if (!mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kWinStages) & 1), err, kErrTimeout, polls))
-      late |= 1u << s0;
+    const int s0 = j % kWinStages, s1 = (j + 1) % kWinStages;
+    // a wait that runs out (in any lane: the warp decides together) stops the slice here, error word set: the
+    // stage is neither read nor refilled, so every stage keeps at most one copy outstanding for the drain below
+    bool ok = mbar_wait_bounded(&bars[s0], static_cast<uint32_t>((j / kWinStages) & 1), err, kErrTimeout, polls);
+    if (pair && ok)
+      ok = mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kWinStages) & 1), err, kErrTimeout, polls);
+    if (!__all_sync(0xffffffffu, ok)) {
+      stop = j;
+      break;
+    }
     uint32_t ka[4][4], va[4][4];
     smem_frags(ka, va, ring + s0 * kStageBytes, ring + s0 * kStageBytes + kTileBytes, lane);
     const int k0 = j * 16;
     if (pair) {
-      const int s1 = (j + 1) % kWinStages;
-      if (!mbar_wait_bounded(&bars[s1], static_cast<uint32_t>(((j + 1) / kWinStages) & 1), err, kErrTimeout, polls))
-        late |= 1u << s1;
       uint32_t kb[4][4], vb[4][4];
       smem_frags(kb, vb, ring + s1 * kStageBytes, ring + s1 * kStageBytes + kTileBytes, lane);
-      consume_frags(ka, va);
-      consume_frags(kb, vb);
-      __syncwarp();
-      if (lane == 0) {  // both stages' operands are in registers: refill them
+      release_stages();
+      if (lane == 0) {  // refill both stages (every lane's reads of them are ordered before the copies)
         if (j + kWinStages < nblk) issue(j + kWinStages);
         if (j + 1 + kWinStages < nblk) issue(j + 1 + kWinStages);
       }
@@ -640,18 +667,24 @@ __global__ void __launch_bounds__(kWinSlices * 32, kWinCtas)
       attend_block2<T, 1>(st, ka, va, kb, vb, qf, ok, scale);
       j += 2;
     } else {
-      consume_frags(ka, va);
-      __syncwarp();
+      release_stages();
       if (lane == 0 && j + kWinStages < nblk) issue(j + kWinStages);
       attend_block<T, 1>(st, ka, va, qf, k0 + g < klen, k0 + g + 8 < klen, scale);
       j += 1;
     }
   }
-  // this slice's state (acc, m, l per query) over the start of its ring: every stage has been consumed (a timed-out
-  // stage's copy may still land there -- the output is invalid then, and the error word says so)
+  if (stop >= 0) {
+    // a timed-out wait: wait (bounded, again) for every copy still outstanding -- blocks stop .. stop + stages - 1,
+    // at most one per stage -- so that no copy lands in the ring after it is reused below or the CTA has exited
+    // (this slice's record is left out: the output is invalid and the error word says so)
+    for (int jj = stop; jj < min(nblk, stop + kWinStages); ++jj)
+      if (!(hold && jj == 0))
+        mbar_wait_bounded(&bars[jj % kWinStages], static_cast<uint32_t>((jj / kWinStages) & 1), nullptr, 0, polls);
+  }
+  // this slice's state (acc, m, l per query) over the start of its ring: every stage has been consumed
   __syncwarp();
   float *rec = reinterpret_cast<float *>(ring);
-  if (late == 0) write_record<1>(st, rec, lane);
+  if (stop < 0) write_record<1>(st, rec, lane);
   __syncthreads();
   // the slices' states -> the output: thread t takes query t / 8, head dims 8 (t % 8) .. + 7 (attn_plugin.py:182-194)
   for (int t = threadIdx.x; t < S * 8; t += blockDim.x) {
@@ -684,12 +717,6 @@ __global__ void __launch_bounds__(kWinSlices * 32, kWinCtas)
     for (int i = 0; i < 8; ++i) num[i] *= inv;
     *reinterpret_cast<uint4 *>(y + (static_cast<size_t>(w) * S + qq) * HD + static_cast<size_t>(h) * kD + 8 * d8) =
         pack8<T>(num);
-  }
-  // a timed-out stage: wait once more (bounded) for its copy before the shared memory goes away
-  for (int j = nblk - min(nblk, kWinStages); j < nblk; ++j) {
-    const int s = j % kWinStages;
-    if (late & (1u << s))
-      mbar_wait_bounded(&bars[s], static_cast<uint32_t>((j / kWinStages) & 1), nullptr, 0, polls);
   }
 }
 

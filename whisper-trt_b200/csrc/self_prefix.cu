@@ -215,8 +215,7 @@ __global__ void __launch_bounds__(kPxWarps * 32)
     const unsigned char *kt = ring + (t % kPxStages) * kPxStage;
     uint32_t ka[4][4], va[4][4];
     smem_frags(ka, va, kt, kt + kPxTile, lane);
-    consume_frags(ka, va);
-    __syncwarp();  // (every lane's reads of this stage are done before any lane refills it)
+    __syncwarp();  // (every lane's reads of this stage before any lane's copies refill it: one proxy, the generic)
     const int k0 = (b0 + t) * 16;
     attend_block_cols<T>(st, ka, va, qf, k0 + g < nb, k0 + g < nb1, k0 + g + 8 < nb, k0 + g + 8 < nb1, scale);
   }
