@@ -69,10 +69,11 @@ int wt_set_launch_flags(int flags);
  * (whose kernels have no device-side waits). */
 unsigned wt_set_wait_limit(unsigned polls);
 /* Test hook for the bounded waits: when nonzero, launches of the fused cross-attention (wt_cross_attn) issue no
- * copy for the first ring stage of their first streaming warp, so that warp's wait on it must run out (after
- * wt_set_wait_limit's polls) and the call's error word is set; no other copy is affected and nothing is left in
- * flight. For tests of the failure path only: 0 (the default) in use. Returns the previous value. No counterpart in
- * the reference. */
+ * copy for the first ring stage of their first streaming warp, and launches of wt_logits32, wt_ln_linear and
+ * wt_linear_residual leave out the row block of the first stage of their first CTA, so a wait on that stage must
+ * run out (after wt_set_wait_limit's polls) and the call's error word is set; every other copy still lands and is
+ * waited for before the kernel exits (nothing is left in flight). For tests of the failure path only: 0 (the
+ * default) in use. Returns the previous value. No counterpart in the reference. */
 int wt_set_test_withhold_stage(int on);
 
 /* ---------------------------------------------------------------------------------------------------------

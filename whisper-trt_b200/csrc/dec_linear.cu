@@ -27,8 +27,10 @@
 //   * ln_linear first normalizes the rows into the workspace with a row kernel; the GEMM is launched after it with
 //     programmatic dependent launch and issues its first stages' weight loads before waiting for it (the weights
 //     are not its output), so the weight stream overlaps the LayerNorm;
-//   * every mbarrier wait is bounded (a timeout records an error in the workspace's device word and the kernel goes
-//     on, then frees its tensor memory).
+//   * every mbarrier wait is bounded: a wait that runs out records an error in the workspace's device word and
+//     raises a stop flag that every role checks, so no role issues more; every CTA still meets its cluster's
+//     barriers, and before it frees its tensor memory the producer waits (bounded) for each copy it issued and the
+//     MMA issuer for its MMAs (a final commit).
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -62,6 +64,7 @@ struct DlArgs {
   void *y;           // [N, V]
   int N, V, kblocks, splits, kb_per, vtiles, nmma, tcols, stages, ring_bytes, res_bytes;
   uint32_t polls;  // bound of every wait (wt_set_wait_limit)
+  int withhold;    // test hook: CTA 0 leaves out the row block of its first stage (wt_set_test_withhold_stage)
 };
 
 // nmma: the rows of a unit (a row chunk; the MMA's N, a multiple of 16). res_bytes: a region after the ring that
@@ -242,7 +245,9 @@ __global__ void __launch_bounds__(kDlThreads)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.ring_bytes + a.res_bytes);
   uint64_t *empty = full + stages;
   uint64_t *acc_full = empty + stages;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_full + 1);
+  uint64_t *drained = acc_full + 1;  // the MMA issuer's last commit: every MMA it issued has completed
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drained + 1);
+  volatile int *stop = reinterpret_cast<volatile int *>(tmem_holder + 1);  // a role's wait ran out
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = a.splits, sp = static_cast<int>(blockIdx.x) % S, t = static_cast<int>(blockIdx.x) / S;
   const int v0 = (t % a.vtiles) * kDlTileV, n0 = (t / a.vtiles) * a.nmma;
@@ -263,6 +268,8 @@ __global__ void __launch_bounds__(kDlThreads)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full[0], 1);
+    mbar_init(drained, 1);
+    *stop = 0;
     fence_mbar_init();
   }
   tc_fence_before();
@@ -274,18 +281,24 @@ __global__ void __launch_bounds__(kDlThreads)
     if (lane == 0) {  // producer: this unit's k blocks through the ring
       // the first stages' weight halves go out before the wait for the preceding kernel (it does not write the
       // weights); their row halves (possibly its output) after it
+      // (the bounded-wait test hook: CTA 0 leaves out the row block of its first stage, whose barrier then never
+      // completes)
+      const bool hold = a.withhold && blockIdx.x == 0;
       bool waited = false;
-      for (int i = 0; i < nkb; ++i) {
+      int i = 0;
+      for (; i < nkb; ++i) {
         const int s = i % stages;
         if (i >= stages) {
           if (!waited) {
             pdl_wait();
             pdl_launch_dependents();
             for (int j = 0; j < stages; ++j)
-              tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
+              if (!(hold && j == 0))
+                tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
             waited = true;
           }
-          mbar_wait_bounded(&empty[s], ((i / stages) - 1) & 1, a.err, kDlErrTimeout, a.polls);
+          if (!mbar_wait_role(&empty[s], ((i / stages) - 1) & 1, a.err, kDlErrTimeout, a.polls, stop))
+            break;  // (nothing more is issued)
         }
         unsigned char *st = smem + s * stage_bytes;
         mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(a_bytes + b_bytes));
@@ -296,8 +309,13 @@ __global__ void __launch_bounds__(kDlThreads)
         pdl_wait();
         pdl_launch_dependents();
         for (int j = 0; j < min(stages, nkb); ++j)
-          tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
+          if (!(hold && j == 0))
+            tma_load_2d(smem + j * stage_bytes + a_bytes, &xmap, (kb0 + j) * kDlKBlock, n0, &full[j]);
       }
+      // every copy issued has landed before the shared memory is reused or goes away: the last fill of each stage
+      // (bounded; at most one outstanding per stage, since a stage is refilled only after its MMAs released it)
+      for (int j = i > stages ? i - stages : 0; j < i; ++j)
+        mbar_wait_bounded(&full[j % stages], (j / stages) & 1, nullptr, 0, a.polls);
     } else {
       pdl_wait();
       pdl_launch_dependents();
@@ -307,9 +325,13 @@ __global__ void __launch_bounds__(kDlThreads)
     pdl_launch_dependents();
     if (lane == 0) {  // MMA issuer
       const uint32_t idesc = idesc_f16(kDlTileV, a.nmma, kBF16);
+      bool halt = false;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
-        mbar_wait_bounded(&full[s], (i / stages) & 1, a.err, kDlErrTimeout, a.polls);
+        if (!mbar_wait_role(&full[s], (i / stages) & 1, a.err, kDlErrTimeout, a.polls, stop)) {
+          halt = true;  // (no MMA reads a stage that has not landed)
+          break;
+        }
         tc_fence_after();
         const uint32_t a_addr = smem_addr(smem + s * stage_bytes), b_addr = a_addr + a_bytes;
         const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(b_addr);
@@ -318,7 +340,10 @@ __global__ void __launch_bounds__(kDlThreads)
           umma_f16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i != 0 || kk != 0) ? 1u : 0u);
         umma_commit(&empty[s]);
       }
-      umma_commit(&acc_full[0]);
+      if (!halt) umma_commit(&acc_full[0]);
+      // every MMA issued has completed before the tensor memory is freed (bounded)
+      umma_commit(drained);
+      mbar_wait_bounded(drained, 0, nullptr, 0, a.polls);
     }
   } else {  // epilogue warps: lane quarter warp % 4 = features v0 + 32 (warp % 4) + lane
     pdl_wait();
@@ -342,12 +367,15 @@ __global__ void __launch_bounds__(kDlThreads)
         }
       }
     }
-    mbar_wait_bounded(&acc_full[0], 0, a.err, kDlErrTimeout, a.polls);
+    // (the warp decides together: its tensor-memory loads are warp-wide; after a timeout it skips them and still
+    // meets the cluster's barriers below)
+    const bool have =
+        __all_sync(0xffffffffu, mbar_wait_role(&acc_full[0], 0, a.err, kDlErrTimeout, a.polls, stop));
     tc_fence_after();
     const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     T *y = static_cast<T *>(a.y);
     float *part = reinterpret_cast<float *>(smem);  // [row][128 features], over the idle ring
-    for (int c0 = 0; c0 < a.nmma; c0 += 64) {  // 64 accumulator columns (rows) per tensor-memory wait
+    for (int c0 = 0; have && c0 < a.nmma; c0 += 64) {  // 64 accumulator columns (rows) per tensor-memory wait
       uint32_t r[4][16];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -653,7 +681,7 @@ int launch_gemm(int dtype, const void *x, const void *w, const void *b, const vo
   st = encode_tile_map(&xm, x, static_cast<unsigned long long>(N), static_cast<unsigned long long>(K), p.nmma, dtype);
   if (st != WT_OK) return st;
   DlArgs a{reinterpret_cast<int *>(workspace), b, res, y, N, V, p.kblocks, p.splits, p.kb_per, p.vtiles, p.nmma,
-           p.tcols, p.stages, p.ring_bytes, p.res_bytes, wait_limit()};
+           p.tcols, p.stages, p.ring_bytes, p.res_bytes, wait_limit(), test_withhold_stage()};
   return launch_clustered("dec_linear", kernel, dim3(p.grid), dim3(kDlThreads), p.smem, stream, p.splits, wm, xm, a);
 }
 

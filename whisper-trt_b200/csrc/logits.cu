@@ -14,8 +14,9 @@
 //     fp32 accumulators in tensor memory) and releases a stage with a tcgen05.commit on its "empty" barrier;
 //   * warps 2-9 drain the accumulators (each warp its lane quarter, warp % 4, and every other 16-column slice), store
 //     them as consecutive floats of each output row and hand the set back;
-//   * every barrier wait is bounded (a timeout records an error in the device word and the kernel goes on, then
-//     frees its tensor memory).
+//   * every barrier wait is bounded: a wait that runs out records an error in the device word and raises a stop flag
+//     that every role checks, so no role issues more; before the CTA frees its tensor memory and exits, the
+//     producer waits (bounded) for each copy it issued and the MMA issuer for its MMAs (a final commit).
 #include <cstdlib>
 
 #include <cuda_bf16.h>
@@ -78,7 +79,7 @@ LgPlan lg_plan(int rows, int vocab, int d_model, int sms) {
   p.stage_bytes = lg_stage_bytes(p.group, p.nmma);
   p.stages = kLgSmemBudget / p.stage_bytes;
   if (p.stages > 8) p.stages = 8;
-  p.smem = 1024 + p.stages * p.stage_bytes + (2 * p.stages + 4) * 8 + 16;
+  p.smem = 1024 + p.stages * p.stage_bytes + (2 * p.stages + 5) * 8 + 16;
   p.grid = p.items < sms ? p.items : sms;
   return p;
 }
@@ -88,7 +89,7 @@ LgPlan lg_plan(int rows, int vocab, int d_model, int sms) {
 template <bool BF16>
 __global__ void __launch_bounds__(kLgThreads)
     logits_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                  float *__restrict__ y, int N, int V, const LgPlan p, int *err, uint32_t polls) {
+                  float *__restrict__ y, int N, int V, const LgPlan p, int *err, uint32_t polls, int withhold) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -99,7 +100,9 @@ __global__ void __launch_bounds__(kLgThreads)
   uint64_t *empty = full + stages;
   uint64_t *acc_full = empty + stages;
   uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *drained = acc_empty + 2;  // the MMA issuer's last commit: every MMA it issued has completed
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drained + 1);
+  volatile int *stop = reinterpret_cast<volatile int *>(tmem_holder + 1);  // a role's wait ran out
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (warp == 0) {
@@ -117,6 +120,8 @@ __global__ void __launch_bounds__(kLgThreads)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kLgEpiWarps);
     }
+    mbar_init(drained, 1);
+    *stop = 0;
     fence_mbar_init();
   }
   tc_fence_before();
@@ -129,8 +134,12 @@ __global__ void __launch_bounds__(kLgThreads)
       // the first item's first stage: its w blocks before the wait for the preceding kernel, its x block after it
       // (one stage: the x block the first MMAs need then waits behind no more w than that; measured faster alone)
       const int pre = static_cast<int>(blockIdx.x) < p.items ? 1 : 0;
+      // (the bounded-wait test hook: CTA 0 leaves out the x block of its first stage, whose barrier then never
+      // completes)
+      const bool hold = withhold && blockIdx.x == 0;
       int it = 0;
-      for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
+      bool halt = false;
+      for (int item = blockIdx.x; item < p.items && !halt; item += gridDim.x) {
         const int t0 = (item / p.chunks) * G, n0 = (item % p.chunks) * nmma;
         const int ng = min(G, p.vtiles - t0);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
@@ -143,11 +152,15 @@ __global__ void __launch_bounds__(kLgThreads)
               pdl_wait();
               pdl_launch_dependents();
               for (int j = 0; j < pre; ++j)
-                tma_load_2d(smem + j * stage_bytes + G * a_bytes, &xmap, j * kLgKBlock, n0, &full[j]);
+                if (!(hold && j == 0))
+                  tma_load_2d(smem + j * stage_bytes + G * a_bytes, &xmap, j * kLgKBlock, n0, &full[j]);
             }
             continue;
           }
-          if (it >= stages) mbar_wait_bounded(&empty[s], ((it / stages) - 1) & 1, err, kLgErrTimeout, polls);
+          if (it >= stages && !mbar_wait_role(&empty[s], ((it / stages) - 1) & 1, err, kLgErrTimeout, polls, stop)) {
+            halt = true;  // (nothing more is issued)
+            break;
+          }
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ng * a_bytes + b_bytes));
           tma_load_2d(st + G * a_bytes, &xmap, kb * kLgKBlock, n0, &full[s]);  // (x first: it is in L2)
           for (int g = 0; g < ng; ++g) tma_load_2d(st + g * a_bytes, &wmap, kb * kLgKBlock, (t0 + g) * kLgTileV, &full[s]);
@@ -157,6 +170,10 @@ __global__ void __launch_bounds__(kLgThreads)
         pdl_wait();
         pdl_launch_dependents();
       }
+      // every copy issued has landed before the shared memory goes away: the last fill of each stage (bounded;
+      // at most one outstanding per stage, since a stage is refilled only after its MMAs released it)
+      for (int i = it > stages ? it - stages : 0; i < it; ++i)
+        mbar_wait_bounded(&full[i % stages], (i / stages) & 1, nullptr, 0, polls);
     } else {
       pdl_wait();
       pdl_launch_dependents();
@@ -167,15 +184,19 @@ __global__ void __launch_bounds__(kLgThreads)
     if (lane == 0) {  // MMA issuer: item j into accumulator set j % nbuf once the epilogue has drained it
       const uint32_t idesc = idesc_f16(kLgTileV, nmma, BF16);
       int it = 0, j = 0;
-      for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++j) {
+      bool halt = false;
+      for (int item = blockIdx.x; item < p.items && !halt; item += gridDim.x, ++j) {
         const int ng = min(G, p.vtiles - (item / p.chunks) * G);
         const int b = j % p.nbuf, use = j / p.nbuf;
-        if (use >= 1) mbar_wait_bounded(&acc_empty[b], (use - 1) & 1, err, kLgErrTimeout, polls);
+        if (use >= 1 && !mbar_wait_role(&acc_empty[b], (use - 1) & 1, err, kLgErrTimeout, polls, stop)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(b * G * p.stride);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % stages;
-          mbar_wait_bounded(&full[s], (it / stages) & 1, err, kLgErrTimeout, polls);
+          if (!mbar_wait_role(&full[s], (it / stages) & 1, err, kLgErrTimeout, polls, stop)) {
+            halt = true;  // (no MMA reads a stage that has not landed)
+            break;
+          }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + s * stage_bytes);
           const uint64_t bdesc = sw128_desc(a_addr + static_cast<uint32_t>(G * a_bytes));
@@ -188,8 +209,11 @@ __global__ void __launch_bounds__(kLgThreads)
           }
           umma_commit(&empty[s]);
         }
-        umma_commit(&acc_full[b]);
+        if (!halt) umma_commit(&acc_full[b]);
       }
+      // every MMA issued has completed before the tensor memory is freed (bounded)
+      umma_commit(drained);
+      mbar_wait_bounded(drained, 0, nullptr, 0, polls);
     }
   } else {  // epilogue warps: lane quarter warp % 4 (vocabulary entries 32 (warp % 4) + lane of each tile), and
             // the 16-column slices c0 = 16 half, 16 half + 32, ... of the rows
@@ -201,7 +225,8 @@ __global__ void __launch_bounds__(kLgThreads)
       const int t0 = (item / p.chunks) * G, n0 = (item % p.chunks) * nmma;
       const int ng = min(G, p.vtiles - t0);
       const int b = j % p.nbuf, use = j / p.nbuf;
-      mbar_wait_bounded(&acc_full[b], use & 1, err, kLgErrTimeout, polls);
+      // (the warp decides together: its tensor-memory loads are warp-wide)
+      if (!__all_sync(0xffffffffu, mbar_wait_role(&acc_full[b], use & 1, err, kLgErrTimeout, polls, stop))) break;
       tc_fence_after();
       for (int g = 0; g < ng; ++g) {
         const int v = (t0 + g) * kLgTileV + quarter * 32 + lane;
@@ -288,5 +313,5 @@ extern "C" int wt_logits32(int dtype, const void *x, const void *w, float *y, in
                         : opt_in_smem<logits_kernel<false>>(p.smem, "logits32");
   if (st != WT_OK) return st;
   return launch("logits32", kernel, dim3(p.grid), dim3(kLgThreads), p.smem, stream, wm, xm, y, rows, vocab, p, err,
-                wait_limit());
+                wait_limit(), test_withhold_stage());
 }

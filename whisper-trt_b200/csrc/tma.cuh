@@ -70,6 +70,24 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   return false;
 }
 
+// The same for the roles of a warp-specialised CTA (a producer, an MMA issuer, epilogue warps) that share a stop flag
+// in shared memory: a wait that runs out records `code` in *err and raises *stop; a wait that sees *stop raised by
+// another role gives up at once, without recording. A role whose wait fails issues nothing more, so the others'
+// waits on it end early instead of each running out its own limit.
+__device__ __forceinline__ bool mbar_wait_role(uint64_t *bar, uint32_t parity, int *err, int code, uint32_t limit,
+                                               volatile int *stop) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) {  // (the flag is read only once the wait is long: the first polls stay as short as a plain wait's)
+      if (*stop) return false;
+      __nanosleep(64);
+    }
+  }
+  if (err != nullptr) atomicExch(err, code);
+  *stop = 1;
+  return false;
+}
+
 // 2D tiled TMA load of the box at (x, y) of `map` into shared memory, completing on `bar` (complete_tx::bytes).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
   asm volatile(
