@@ -111,6 +111,27 @@ def test_stream_kernel_repeated_launches(w, s):
     assert all(torch.equal(y, outs[0]) for y in outs)  # (and every launch gives the same bits)
 
 
+@pytest.mark.parametrize("w,s", [(8, 5), (32, 5), (16, 8), (3, 1)])
+def test_window_kernel_repeated_launches(w, s):
+    """At most 8 queries per window take the one-CTA-per-(window, head) kernel; 20 launches each match the oracle
+    and give the same bits (its TMA rings are refilled while the warps still compute, as the stream-K kernel's)."""
+    q, k, v = rand_cross(w, s, 20, 1500, torch.float16, seed=200 * w + s)
+    ref = torch.from_numpy(oa.cross_attn(*oracle_inputs(q, k, v))).cuda()
+    outs = [ap.cross_attn_triton(q, k, v) for _ in range(20)]
+    assert max(float((y.float() - ref).abs().max()) for y in outs) <= ATOL
+    assert all(torch.equal(y, outs[0]) for y in outs)
+
+
+@pytest.mark.parametrize("w,s", [(32, 5), (8, 5), (4, 16)])
+def test_split_repeated_launches(w, s):
+    """The reference-shaped split (8 key slices per (window, head), on the stream-K kernel in slice mode): 20
+    launches give the same partials, and their combine matches the oracle."""
+    q, k, v = rand_cross(w, s, 20, 1500, torch.float16, seed=300 * w + s)
+    parts = [ap.cross_attn_split_triton(q, k, v) for _ in range(20)]
+    assert all(torch.equal(p, parts[0]) for p in parts)
+    assert_close(ap.cross_attn_combine_triton(parts[0], q), oa.cross_attn(*oracle_inputs(q, k, v)))
+
+
 @pytest.mark.parametrize("w", [1, 8, 32])
 def test_whisper_shapes(w):
     """20 heads x 64 over 1500 frames, beam 5 (configs 2 / 3 per layer) -- fused and split paths."""
