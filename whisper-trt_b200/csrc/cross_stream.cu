@@ -582,14 +582,20 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, kCtas)
 // leaves the SM and no counter is taken: the tail after the last block is a few hundred cycles (the stream-K and
 // slice-unit kernels end with a partial's stores, a GPU-scope count and an L2 round trip per combined slice). With
 // programmatic dependent launch the first stages' loads go out before the wait for the preceding kernel.
-// Shapes (slices = warps per CTA, ring stages per warp, CTAs per SM); WT_CROSS_WIN_SHAPE (a tuning knob) picks one.
-// Measured per launch chained at 32 windows (config 2 / config 5 step): (8, 3, 2) 44.3 us (572 / 4516 us); (16, 2, 1)
-// 45.3 (661 / 4633); (16, 3, 1) 46.2 (678 / 4743); (12, 3, 1) 46.2 (668 / 4776) -- finer slices do not pay for the
-// single CTA per SM.
+// Shapes (slices = warps per CTA, ring stages per warp, CTAs per SM: shared memory allows no more). The launch takes
+// the shape whose whole waves of CTAs waste the fewest unit slots (window_shape_for), as measured on B200 per launch
+// chained (same kernel back to back) at 8 / 16 / 24 / 32 / 64 windows of 20 heads x 1500 frames: (8, 3, 2) 16.6 /
+// 30.4 / 35.0 / 48.1 / 81.1 us; (4, 4, 3) 17.4 / 24.8 / 43.2 / 45.3 / 78.5; (4, 3, 4) 18.6 / 24.8 / 33.3 / 52.0 / 84.8
+// -- a launch whose last wave is a small fraction of the resident CTAs pays for it (24 windows on (4, 4, 3), 32 on
+// (4, 3, 4)); the decode step at 32 windows (config 3) 2.033 -> 1.913 ms on (4, 4, 3), at 16 windows (config 4)
+// 1.350 -> 1.244 ms, at 8 windows (config 2) 0.579 -> 0.647 ms (so (8, 3, 2) there). Also measured, slower at every
+// size: (16, 2, 1), (16, 3, 1), (12, 3, 1), (6, 4, 2), (4, 6, 2), (5, 5, 2), (6, 3, 2), and 3 CTAs of 6-12 warps
+// (registers spill). WT_CROSS_WIN_SHAPE (a tuning knob) forces one.
 struct WinShape {
   int slices, stages, ctas;
 };
-constexpr WinShape kWinShapes[] = {{8, 3, 2}, {16, 2, 1}};
+constexpr WinShape kWinShapes[] = {{8, 3, 2}, {16, 2, 1}, {4, 4, 3}, {4, 3, 4}};
+constexpr int kNumWinShapes = static_cast<int>(sizeof(kWinShapes) / sizeof(kWinShapes[0]));
 constexpr int win_smem(int slices, int stages) { return slices * stages * kStageBytes + slices * stages * 8 + 1024; }
 
 template <typename T, int kWinSlices, int kWinStages, int kWinCtas>
@@ -744,17 +750,38 @@ struct StreamPlan {
 };
 
 // The one-CTA-per-(window, head) kernel takes the fused attention when a window has at most 8 queries (one query
-// tile) and every 16-key block of the 8 slices holds a key; the stream-K kernel the rest. Measured per launch, chained
+// tile) and every 16-key block of the chosen shape's slices holds a key; the stream-K kernel the rest. Measured per launch, chained
 // as in the step (stream-K -> this kernel): 8 windows 14.3 -> 13.3 us, 32 windows 44.2 -> 43.7 us, 64 windows 91.6 ->
 // 78.1 us (the CTAs' dynamic scheduling leaves a smaller tail than the stream-K ranges' unit-boundary combines).
 // WT_CROSS_WINDOW=0 (a tuning knob) turns it off.
-int window_shape() {
+int forced_window_shape() {
   static const int idx = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_CROSS_WIN_SHAPE");
-    const int v = e ? atoi(e) : 0;
-    return (v >= 0 && v < static_cast<int>(sizeof(kWinShapes) / sizeof(kWinShapes[0]))) ? v : 0;
+    const int v = e ? atoi(e) : -1;
+    return (v >= 0 && v < kNumWinShapes) ? v : -1;
   }();
   return idx;
+}
+
+// The window kernel's shape for W x H (window, head) units over Tn frames, or -1 if none fits (some 16-key block of a
+// slice would hold no key): among (4, 4, 3), (4, 3, 4) and (8, 3, 2), in that order of preference on ties, the one
+// whose whole waves -- ceil(units / resident CTAs) x resident CTAs -- leave the fewest slots idle.
+int window_shape_for(int W, int H, int Tn) {
+  const int forced = forced_window_shape();
+  if (forced >= 0) return cross_stream_slices_ok(Tn, kWinShapes[forced].slices) ? forced : -1;
+  const long long units = static_cast<long long>(W) * H;
+  int best = -1;
+  long long best_slots = 0;
+  for (const int i : {2, 3, 0}) {
+    if (!cross_stream_slices_ok(Tn, kWinShapes[i].slices)) continue;
+    const long long resident = static_cast<long long>(sm_count()) * kWinShapes[i].ctas;
+    const long long slots = (units + resident - 1) / resident * resident;
+    if (best < 0 || slots < best_slots) {
+      best = i;
+      best_slots = slots;
+    }
+  }
+  return best;
 }
 
 bool window_kernel_ok(int W, int S, int H, int Tn) {
@@ -762,7 +789,7 @@ bool window_kernel_ok(int W, int S, int H, int Tn) {
     const char *e = getenv("WT_CROSS_WINDOW");
     return (e != nullptr && atoi(e) == 0) ? 1 : 0;
   }();
-  return !off && W > 0 && H > 0 && S <= 8 && cross_stream_slices_ok(Tn, kWinShapes[window_shape()].slices);
+  return !off && W > 0 && H > 0 && S <= 8 && window_shape_for(W, H, Tn) >= 0;
 }
 
 template <typename T, int SL, int ST, int CT>
@@ -780,13 +807,15 @@ int launch_window_shape(const CUtensorMap &km, const CUtensorMap &vm, const void
 template <typename T>
 int launch_window(const CUtensorMap &km, const CUtensorMap &vm, const void *q, void *y, int *err, int W, int S,
                   int H, int Tn, float scale, void *stream) {
-  switch (window_shape()) {
+  switch (window_shape_for(W, H, Tn)) {
 #define WT_WIN_CASE(i)                                                                                           \
   case i:                                                                                                        \
     return launch_window_shape<T, kWinShapes[i].slices, kWinShapes[i].stages, kWinShapes[i].ctas>(km, vm, q, y, err, \
                                                                                                  W, S, H, Tn, scale, \
                                                                                                  stream);
     WT_WIN_CASE(1)
+    WT_WIN_CASE(2)
+    WT_WIN_CASE(3)
 #undef WT_WIN_CASE
     default:
       return launch_window_shape<T, kWinShapes[0].slices, kWinShapes[0].stages, kWinShapes[0].ctas>(km, vm, q, y, err,
