@@ -1,5 +1,5 @@
 // Fused cross-attention (split + combine in one launch), fed by TMA: a window of at most 8 queries (a beam or a
-// sample group) takes cross_window_kernel below -- one CTA per (window, head), 8 key slices combined in shared
+// sample group) takes cross_window_kernel below -- one CTA per (window, head), 4 or 8 key slices combined in shared
 // memory; larger query groups, and the reference-shaped split (slice mode), take the persistent stream-K kernel.
 //
 // Semantics: the reference's cross_attn (attn_plugin.py:129-136, kernel :352-376) -- softmax(q k^T / sqrt(D)) v per
