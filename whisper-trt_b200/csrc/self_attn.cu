@@ -12,9 +12,8 @@
 //     row's chain of dependent loads is a quarter as long as with one warp per (row, head), and the many short
 //     CTAs balance over the SMs by themselves;
 //   * each warp streams stages of (32 / LPK) * U keys through an S-deep cp.async ring (16-byte copies, bypassing
-//     L1; head_dim 64 with up to 256 slots per split: U = 2, S = 3, 24 KB of rings per CTA keep 8 CTAs on an SM;
-//     else U = 4, S = 2): the loads in flight hold no registers, and the ring is laid out piece-major
-//     ([piece][lane]) so every read-back is bank-conflict free;
+//     L1; head_dim 64: U = 2, S = 2, 16 KB of rings per CTA): the loads in flight hold no registers, and the ring
+//     is laid out piece-major ([piece][lane]) so every read-back is bank-conflict free;
 //   * a key row is covered by LPK lanes (D/8 by default: one 16-byte piece each), dot products on mixed-precision
 //     FMAs (half/bf16 products accumulated in fp32) finished with butterfly shuffles; each group of LPK lanes runs
 //     its own online softmax (U keys per stage); groups merge by shuffles, the 4 warps through shared memory;
@@ -438,22 +437,22 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
                 static_cast<T *>(y), part, counters, N, H, C, write_cache, splits, scale, group, min_shared, xrec);
 }
 
-// Shape (lanes per key row, keys per lane group per stage, stages) of the head_dim 64 kernel. By default it follows
-// the cache slots per split: up to 256, (8, 2, 3) -- 24 KB of rings per CTA keep 8 CTAs on an SM while 16 keys per
-// warp are in flight before the wait for the preceding kernel (measured per step: 1980 -> 1924 us at 160 rows, C
-// 228; 670 -> 666 us at 40 rows); above, (8, 4, 2) -- long rows want 32 keys per warp in flight (1589 us at 80 rows,
-// C 448, lengths U[224, 447], against 1674 with (8, 2, 3)). Four lanes per key row with two 16-byte pieces each,
-// (4, 1, 3), time the same at 160 rows, C 228 (18.6 us per launch chained; (4, 2, 2) 20.3, (4, 2, 3) 23.6 and
-// (2, 1, 2) 29.5): the kernel is bound by its loads' latency, not by the shuffles and FMAs per key. WT_SELF_SHAPE (a
-// tuning knob) forces 0 = (8, 4, 2), 1 = (8, 2, 2), 2 = (8, 2, 3), 3 = (8, 1, 4) or 4 = (4, 1, 3).
-int self_shape(int cap) {
+// Shape (lanes per key row, keys per lane group per stage, stages) of the head_dim 64 kernel: (8, 2, 2) -- 16 KB of
+// rings per CTA, 16 keys per warp in flight. Measured per decode step beside the 4-warp cross-attention shape
+// (3 CTAs of 66.7 KB per SM): 160 rows, C 228: 1896 us against 1908 for (8, 2, 3), 1951 for (8, 4, 2), 1959 for
+// (8, 1, 4), 1926 for (4, 1, 3); 80 rows, C 448, lengths U[224, 447] with the shared prefix: 1163 us against 1240
+// (8, 2, 3) and 1244 (8, 4, 2); 320 rows, C 448: 4415 against 4440; 40 rows: 583 against 579. (Beside the earlier
+// 8-warp cross shape, whose CTAs took 99.5 KB each, (8, 2, 3) at C <= 256 and (8, 4, 2) above had measured best.)
+// Four lanes per key row with two 16-byte pieces each time about the same: the kernel is bound by its loads'
+// latency, not by the shuffles and FMAs per key. WT_SELF_SHAPE (a tuning knob) forces 0 = (8, 4, 2), 1 = (8, 2, 2),
+// 2 = (8, 2, 3), 3 = (8, 1, 4) or 4 = (4, 1, 3).
+int self_shape() {
   static const int forced = [] {  // (read once; a function-local static initialises thread-safely)
     const char *e = getenv("WT_SELF_SHAPE");
     const int x = e ? atoi(e) : -1;
     return (x >= 0 && x <= 4) ? x : -1;
   }();
-  if (forced >= 0) return forced;
-  return cap <= 256 ? 2 : 0;
+  return forced >= 0 ? forced : 1;
 }
 
 template <typename T>
@@ -467,7 +466,7 @@ int dispatch_step(int D, const void *qkv, void *kc, void *vc, const int64_t *off
     case 16: return WT_STEP(16, 2, 4, 2);
     case 32: return WT_STEP(32, 4, 4, 2);
     case 64:
-      switch (self_shape((C + splits - 1) / splits)) {
+      switch (self_shape()) {
         case 1: return WT_STEP(64, 8, 2, 2);
         case 2: return WT_STEP(64, 8, 2, 3);
         case 3: return WT_STEP(64, 8, 1, 4);
