@@ -29,7 +29,7 @@ def _call(lib, q, k, v, ws):
     return y
 
 
-@pytest.mark.parametrize("windows,S", [(2, 5), (32, 5), (4, 16)])  # (window kernel; 16 queries: stream-K kernel)
+@pytest.mark.parametrize("windows,S", [(2, 5), (32, 5), (24, 5), (4, 16)])  # (window kernel, its 3 shapes; stream-K)
 def test_cross_attn_wait_runs_out_then_recovers(windows, S):
     lib = _lib.load()
     g = torch.Generator().manual_seed(windows)

@@ -111,10 +111,12 @@ def test_stream_kernel_repeated_launches(w, s):
     assert all(torch.equal(y, outs[0]) for y in outs)  # (and every launch gives the same bits)
 
 
-@pytest.mark.parametrize("w,s", [(8, 5), (32, 5), (16, 8), (3, 1)])
+@pytest.mark.parametrize("w,s", [(8, 5), (32, 5), (16, 8), (3, 1), (24, 5)])
 def test_window_kernel_repeated_launches(w, s):
     """At most 8 queries per window take the one-CTA-per-(window, head) kernel; 20 launches each match the oracle
-    and give the same bits (its TMA rings are refilled while the warps still compute, as the stream-K kernel's)."""
+    and give the same bits (its TMA rings are refilled while the warps still compute, as the stream-K kernel's).
+    The launch picks its shape by the window count: 8 warps x 3 stages at 3 and 8 windows, 4 x 4 at 16 and 32,
+    4 x 3 (4 CTAs per SM) at 24."""
     q, k, v = rand_cross(w, s, 20, 1500, torch.float16, seed=200 * w + s)
     ref = torch.from_numpy(oa.cross_attn(*oracle_inputs(q, k, v))).cuda()
     outs = [ap.cross_attn_triton(q, k, v) for _ in range(20)]
