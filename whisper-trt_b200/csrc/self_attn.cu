@@ -443,8 +443,8 @@ int launch_step(const void *qkv, void *kc, void *vc, const int64_t *offset, cons
 // (8, 1, 4), 1926 for (4, 1, 3); 80 rows, C 448, lengths U[224, 447] with the shared prefix: 1163 us against 1240
 // (8, 2, 3) and 1244 (8, 4, 2); 320 rows, C 448: 4415 against 4440; 40 rows: 583 against 579. (Beside the earlier
 // 8-warp cross shape, whose CTAs took 99.5 KB each, (8, 2, 3) at C <= 256 and (8, 4, 2) above had measured best.)
-// Four lanes per key row with two 16-byte pieces each time about the same: the kernel is bound by its loads'
-// latency, not by the shuffles and FMAs per key. WT_SELF_SHAPE (a tuning knob) forces 0 = (8, 4, 2), 1 = (8, 2, 2),
+// Also slower at config 3: (4, 1, 2) 1938, (4, 2, 2) 1994, (8, 1, 2) 1968, (8, 1, 3) 1961 us (fewer keys in flight
+// per warp, or four lanes per key row with two 16-byte pieces each). WT_SELF_SHAPE (a tuning knob) forces 0 = (8, 4, 2), 1 = (8, 2, 2),
 // 2 = (8, 2, 3), 3 = (8, 1, 4) or 4 = (4, 1, 3).
 int self_shape() {
   static const int forced = [] {  // (read once; a function-local static initialises thread-safely)
