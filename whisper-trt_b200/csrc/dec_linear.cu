@@ -581,7 +581,10 @@ int max_clusters(Kern kernel, int splits, int smem) {
   static int used = 0;
   static std::mutex mu;
   int dev = 0;
-  cudaGetDevice(&dev);
+  if (cudaGetDevice(&dev) != cudaSuccess) {  // (no device to key the cache by: assume every SM holds one CTA)
+    cudaGetLastError();
+    return dl_sm_count() / splits;
+  }
   const void *kp = reinterpret_cast<const void *>(kernel);
   {
     std::lock_guard<std::mutex> lock(mu);
